@@ -1,0 +1,184 @@
+/*
+ * tla_api.h - C ABI of the B200 attention path for three-llm.
+ *
+ * This is the boundary a three-llm host binds (N-API addon, FFI or ctypes) in
+ * place of the WebGPU operator `TSLAttention`
+ * (packages/three-llm/src/tsl/TSLAttention.ts:19-448). Plain C types only:
+ * device buffers are `void*` / typed pointers that the caller owns, streams
+ * are `cudaStream_t` passed as `void*` (NULL = legacy default stream).
+ * Every call returns a tla_status (0 = ok, < 0 = error); nothing throws.
+ *
+ * Threading: a tla_ctx (and every layer made from it) is used from one host
+ * thread and one CUDA stream at a time. Calls are stream-ordered and do not
+ * block, except tla_cache_read/tla_cache_write/tla_get_error, which
+ * synchronise the device.
+ */
+#ifndef TLA_API_H
+#define TLA_API_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The RoPE codes carry the reference's error messages
+ * (packages/three-llm/src/runtime/rope.ts:5-41); tla_status_string returns them. */
+typedef enum tla_status {
+  TLA_OK = 0,
+  TLA_ERR_INVALID_ARG = -1,
+  TLA_ERR_ROPE_DIM = -2,      /* RoPE dimension must be a non-negative even integer. (rope.ts:5-6) */
+  TLA_ERR_ROPE_THETA = -3,    /* RoPE theta must be finite and greater than one. (rope.ts:7) */
+  TLA_ERR_ROPE_FACTOR = -4,   /* RoPE scaling factor must be finite and at least one. (rope.ts:14-15) */
+  TLA_ERR_YARN_RANGE = -5,    /* Invalid YaRN context or beta range. (rope.ts:17-20) */
+  TLA_ERR_YARN_FACTOR = -6,   /* Invalid YaRN attention factor. (rope.ts:22) */
+  TLA_ERR_LLAMA3_RANGE = -7,  /* Invalid Llama 3 RoPE frequency range. (rope.ts:38-41) */
+  TLA_ERR_ROTARY_DIM = -8,    /* Invalid rotary dimension (load/DecoderRecipe.ts:409-415) */
+  TLA_ERR_UNSUPPORTED = -9,   /* shape outside what the kernels implement */
+  TLA_ERR_CUDA = -10,         /* a CUDA runtime call failed */
+  TLA_ERR_OUT_OF_MEMORY = -11,
+  TLA_ERR_POSITION = -12,     /* device-reported: a position outside [0, max_tokens) */
+  TLA_ERR_TIMEOUT = -13,      /* device-reported: a bounded in-kernel wait expired */
+  TLA_ERR_NO_DEVICE = -14,
+  TLA_ERR_SHARED = -15        /* operation not allowed on a layer that borrows another's cache */
+} tla_status;
+
+/* RoPE scaling: RopeScalingConfig | YarnRoPEConfig (packages/three-llm/src/types.ts:245-256). */
+typedef enum tla_rope_type {
+  TLA_ROPE_NONE = 0,
+  TLA_ROPE_LINEAR = 1,
+  TLA_ROPE_YARN = 2,
+  TLA_ROPE_LLAMA3 = 3
+} tla_rope_type;
+
+typedef struct tla_rope_scaling {
+  int32_t type;                   /* tla_rope_type */
+  double factor;
+  double original_context_length; /* yarn, llama3 */
+  double beta_fast, beta_slow;    /* yarn */
+  int32_t has_attention_factor;   /* yarn: 0 => 1 + 0.1*ln(factor) */
+  double attention_factor;
+  double low_freq_factor, high_freq_factor; /* llama3 */
+} tla_rope_scaling;
+
+/* Flag bits of tla_attn_config.flags */
+enum {
+  TLA_FLAG_OFFSET_RMS_NORM = 1u << 0, /* offsetRMSNorm: QK-norm scale is (1 + w) */
+  TLA_FLAG_V_NORM = 1u << 1,          /* vNorm: weightless RMS norm of V before caching */
+  TLA_FLAG_IO_FP32 = 1u << 2,         /* qkv, gate and out are float32 (default: fp16) */
+  TLA_FLAG_CACHE_FP32 = 1u << 3       /* K/V cache in float32 (default: fp16) */
+};
+
+/* AttentionKernelOptions (packages/three-llm/src/types.ts:288-312) plus the
+ * TSLAttention constructor's sizes (TSLAttention.ts:64-70). */
+typedef struct tla_attn_config {
+  int32_t head_count;      /* headCount */
+  int32_t kv_head_count;   /* kvHeadCount; 0 => head_count */
+  int32_t head_dim;        /* headDim */
+  int32_t max_tokens;      /* maxTokens: cache slots per sequence */
+  int32_t max_batch;       /* sequences the cache holds (the reference has one) */
+  int32_t rotary_dim;      /* rotaryDim; -1 => head_dim */
+  int32_t rope_freq_dim;   /* ropeFreqDim; 0 => rotary_dim */
+  int32_t rope_pair_count; /* ropePairCount; -1 => rotary_dim / 2 */
+  double rope_theta;       /* ropeTheta; 0 disables RoPE */
+  tla_rope_scaling rope_scaling; /* ropeScaling ?? yarn; type NONE => none */
+  int32_t sliding_window;  /* slidingWindow; 0 => none */
+  int32_t has_attn_scale;  /* 0 => attnScale = 1/sqrt(head_dim) */
+  double attn_scale;
+  double rms_epsilon;      /* rmsEpsilon; 0 => 1e-6 */
+  uint32_t flags;          /* TLA_FLAG_* */
+} tla_attn_config;
+
+typedef struct tla_ctx tla_ctx;
+typedef struct tla_layer tla_layer;
+
+/* Physical cache view (for zero-copy host bindings and tests). Element
+ * (seq, kv_head, token, d) lives at base + seq*seq_stride + kv_head*head_stride
+ * + token*token_stride + d, strides in elements. */
+typedef struct tla_cache_view {
+  void* key;
+  void* value;
+  int64_t seq_stride, head_stride, token_stride;
+  int32_t elem_bytes;      /* 2 (fp16) or 4 (fp32) */
+} tla_cache_view;
+
+const char* tla_status_string(int status);
+
+/* Context: one per device. Owns the error word and the split-KV scratch. */
+int tla_create(int device, tla_ctx** out);
+int tla_destroy(tla_ctx* ctx);
+
+/* Device-reported errors since the last reset (synchronises the device).
+ * Replaces the reference's absence of a GPU error channel. */
+int tla_get_error(tla_ctx* ctx, int reset);
+
+/* ropeParameters (packages/three-llm/src/runtime/rope.ts:4-52):
+ * inv_freq[dim/2] float32 and the YaRN attention factor. */
+int tla_rope_parameters(int32_t dim, double theta, const tla_rope_scaling* scaling, float* inv_freq,
+                        double* attention_factor);
+
+/* new TSLAttention(qkv, hiddenSize, headCount, maxTokens, options)
+ * (TSLAttention.ts:64-166). q_norm_weight / k_norm_weight: host float32
+ * [head_dim] or NULL (qNormWeight / kNormWeight). Allocates and zeroes the
+ * K/V cache [max_batch][kv_head_count][max_tokens][head_dim]. */
+int tla_layer_create(tla_ctx* ctx, const tla_attn_config* config, const float* q_norm_weight,
+                     const float* k_norm_weight, tla_layer** out);
+/* sharedAttention (TSLAttention.ts:122-139): dst reads src's cache and
+ * stops appending to it (no copy step, TSLAttention.ts:154-156). Shapes must match. */
+int tla_layer_share_cache(tla_layer* dst, const tla_layer* src);
+int tla_layer_destroy(tla_layer* layer);
+int tla_layer_cache_view(const tla_layer* layer, tla_cache_view* view);
+
+/* One decode step for `batch` sequences (TSLAttention.compute, TSLAttention.ts:443-447,
+ * with its four kernels fused: copy-KV :252-286, query :288-304, scores :306-356,
+ * softmax+PV :358-428).
+ *   qkv       device [batch][head_count + 2*kv_head_count][head_dim]  ([Q | K | V])
+ *   positions device int32 [batch]: the new token's position (positionNode)
+ *   gate      device [batch][head_count][head_dim] or NULL (gateNode: out *= sigmoid(gate))
+ *   out       device [batch][head_count][head_dim]
+ * The new K (after QK-norm and RoPE) and V are written to slot positions[b]. */
+int tla_decode(tla_layer* layer, const void* qkv, const int32_t* positions, const void* gate, void* out,
+               int32_t batch, void* stream);
+
+/* Causal prefill of seq_len tokens per sequence starting at start_pos[b]:
+ * equal to seq_len decode steps at start_pos[b] + t
+ * (DecoderTSLRunner.prefillTokens, packages/three-llm/src/decoder/DecoderTSLRunner.ts:504-530).
+ *   qkv device [batch][seq_len][head_count + 2*kv_head_count][head_dim]
+ *   out device [batch][seq_len][head_count][head_dim]
+ *   start_pos device int32 [batch] */
+int tla_prefill(tla_layer* layer, const void* qkv, const int32_t* start_pos, int32_t seq_len, void* out,
+                int32_t batch, void* stream);
+
+/* Sequence-sharded decode building block: attend over cache slots
+ * [0, local_tokens) that hold global positions [slot_offset, slot_offset +
+ * local_tokens), and emit per query head the partial triple
+ * partial[b][h] = {m (log2 domain), l, o[head_dim] (unnormalised)} as float32
+ * [batch][head_count][head_dim + 2]. If append != 0 the new token (global
+ * position positions[b]) is written to slot positions[b] - slot_offset and
+ * included. Slots outside [window start, positions[b]] are excluded. */
+int tla_decode_partial(tla_layer* layer, const void* qkv, const int32_t* positions, int32_t slot_offset,
+                       int32_t local_tokens, int32_t append, float* partial, int32_t batch, void* stream);
+
+/* Log-sum-exp merge of `ranks` partial triples laid out
+ * [ranks][batch][head_count][head_dim + 2] into out [batch][head_count][head_dim]
+ * (fp16, or float32 with TLA_FLAG_IO_FP32 in io_flags), times sigmoid(gate) if gate != NULL. */
+int tla_combine_lse(const float* partials, int32_t ranks, int32_t batch, int32_t head_count, int32_t head_dim,
+                    const void* gate, void* out, uint32_t io_flags, void* stream);
+
+/* reset() (TSLAttention.ts:434-441): zero the cache. A borrowing layer is a no-op. */
+int tla_cache_reset(tla_layer* layer, void* stream);
+
+/* Test / binding view of the cache as the reference lays it out
+ * (token-major float32 [count][kv_head_count*head_dim], TSLAttention.ts:120):
+ * keyCacheAttribute / valueCacheAttribute. Synchronises. NULL outputs skip. */
+int tla_cache_read(const tla_layer* layer, int32_t seq, int32_t token_begin, int32_t count, float* key_out,
+                   float* value_out);
+/* Inverse of tla_cache_read: host float32 token-major rows into the cache. */
+int tla_cache_write(tla_layer* layer, int32_t seq, int32_t token_begin, int32_t count, const float* key,
+                    const float* value);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TLA_API_H */

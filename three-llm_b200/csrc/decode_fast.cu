@@ -1,0 +1,656 @@
+// Persistent split-KV decode attention for B200 (sm_100a), fp16 K/V cache,
+// head_dim 64 or 128, GQA group <= 16.
+//
+// Replaces the four WebGPU kernels of one TSLAttention decode step
+// (packages/three-llm/src/tsl/TSLAttention.ts:252-428): copy-KV (RoPE and
+// QK-norm of the new K, append), query (RoPE and QK-norm of Q), scores and the
+// two-pass softmax + PV. Semantics follow causalAttention
+// (packages/three-llm/src/runtime/math.ts:179-276).
+//
+// Work split: the (sequence, kv head) pairs' token ranges are cut into
+// 64-token tiles; the grid is persistent (a fixed number of CTAs per SM) and
+// CTA c takes the contiguous global tile range [c*T/C, (c+1)*T/C), so every
+// CTA streams the same number of bytes whatever the per-sequence lengths.
+// A CTA's range may start or end inside a pair: such partial segments leave
+// (m, l, o) triples in scratch, and the CTA that completes a pair's tile count
+// (an atomic ticket, no spinning) merges them with a log-sum-exp combine.
+//
+// CTA: 4 consumer warps + 1 producer warp. The producer's lane 0 streams K and
+// V tiles with TMA (cp.async.bulk.tensor, 128-byte swizzle) into a ring of
+// shared-memory stages guarded by mbarriers. Each consumer warp owns 16 tokens
+// of a tile: S = Q K^T and O += P V run as m16n8k16 tensor-core tiles (the
+// GQA group's query heads are the 16 rows), the online softmax keeps fp32
+// running max / sum per row, reduced across the 4 lanes that share a row with
+// warp shuffles. All smem reads are ldmatrix on the swizzled layout.
+#include <math.h>
+
+#include "tla_device.cuh"
+#include "tla_internal.h"
+
+namespace tla {
+
+namespace {
+
+constexpr int kTile = 64;            // tokens per pipeline stage
+constexpr int kConsumerWarps = 4;    // 16 tokens each
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxBatch = 1024;      // prefix table in shared memory
+
+template <int D>
+struct Cfg {
+  static constexpr int kStages = D == 64 ? 4 : 3;
+  static constexpr int kBoxes = D / 64;                      // 64-element TMA boxes per row
+  static constexpr int kBoxBytes = kTile * 128;              // one [64 tok][64 el] fp16 box
+  static constexpr int kTileBytes = kBoxes * kBoxBytes;      // K (or V) of one tile
+  static constexpr int kStageBytes = 2 * kTileBytes;         // K + V
+  static constexpr int kQPitch = D * 2 + 16;                 // padded row pitch of the Q tile
+  static constexpr int kMinBlocks = D == 64 ? 3 : 2;
+};
+
+struct DecodeParams {
+  CUtensorMap tmap_k;
+  CUtensorMap tmap_v;
+  LayerArgs a;
+  const void* qkv;
+  const int32_t* positions;
+  const void* gate;
+  void* out;
+  float* partial_out;  // sequence-shard mode: [B][Hq][D + 2]; null => out
+  float* scratch;      // [grid][2][G][D + 2]
+  int32_t* counters;   // [B * Hk], zero between launches
+  int batch, slot_offset, local_tokens, append;
+};
+
+struct SmemLayout {
+  // byte offsets from the 1024-aligned base
+  int stages, q, qf, kvf, cs, newkv, red, prefix, bars, flags, total;
+};
+
+template <int D>
+__host__ __device__ inline SmemLayout smem_layout(int G, int batch) {
+  using C = Cfg<D>;
+  SmemLayout s;
+  int off = 0;
+  s.stages = off;
+  off += C::kStages * C::kStageBytes;
+  s.q = off;
+  off += 16 * C::kQPitch;
+  s.qf = off;
+  off += 16 * D * 4;
+  s.kvf = off;
+  off += 2 * D * 4;
+  s.cs = off;
+  off += D * 4;  // cos[D/2], sin[D/2]
+  s.newkv = off;
+  off += 2 * D * 2;
+  s.red = off;
+  off += kConsumerWarps * G * (D + 2) * 4;
+  s.prefix = off;
+  off += (batch + 1) * 4;
+  off = (off + 7) & ~7;
+  s.bars = off;
+  off += 2 * C::kStages * 8;
+  s.flags = off;
+  off += 16;
+  s.total = off + 1024;  // alignment slack
+  return s;
+}
+
+// Local slot range [lo, hi] a sequence attends over (math.ts:208 window,
+// sequence-shard clipping), or lo > hi if empty.
+__device__ __forceinline__ void seq_range(const LayerArgs& a, int pos, int slot_offset, int local_tokens, int* lo,
+                                          int* hi) {
+  const int first = a.sliding > 0 ? max(0, pos - a.sliding + 1) : 0;
+  *lo = max(first, slot_offset) - slot_offset;
+  *hi = min(pos, slot_offset + local_tokens - 1) - slot_offset;
+}
+
+__device__ __forceinline__ long long cta_begin(int c, long long total, int grid) {
+  return (static_cast<long long>(c) * total) / grid;
+}
+
+// Largest c with cta_begin(c) <= g.
+__device__ __forceinline__ int cta_of(long long g, long long total, int grid) {
+  int c = static_cast<int>((g * grid) / total);
+  while (c + 1 < grid && cta_begin(c + 1, total, grid) <= g) ++c;
+  while (c > 0 && cta_begin(c, total, grid) > g) --c;
+  return c;
+}
+
+template <int D, typename IO, bool TWO_ROWS>
+__global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
+    decode_fast_kernel(const __grid_constant__ DecodeParams p) {
+  using C = Cfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const LayerArgs& a = p.a;
+  const int G = a.G, Hk = a.Hk, Hq = a.Hq;
+  const SmemLayout L = smem_layout<D>(G, p.batch);
+  int* prefix = reinterpret_cast<int*>(smem + L.prefix);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + C::kStages;
+  volatile int* flags = reinterpret_cast<volatile int*>(smem + L.flags);  // [0] abort, [1] last-CTA ticket
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grid = gridDim.x, cta = blockIdx.x;
+
+  // ---- partition: tiles per sequence, prefix over (sequence, kv head) pairs
+  for (int b = tid; b < p.batch; b += kThreads) {
+    const int pos = p.positions[b];
+    int tiles = 0;
+    int lo, hi;
+    seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
+    // With append, the new token must be the last local slot (always true
+    // for plain decode, where the local range is the whole cache).
+    const bool ok = pos >= 0 && (p.partial_out != nullptr || pos < a.max_tokens) &&
+                    (!p.append || (pos - p.slot_offset >= 0 && pos - p.slot_offset < a.max_tokens &&
+                                   pos - p.slot_offset == hi));
+    if (ok) {
+      if (hi >= lo) tiles = (hi - lo + kTile) / kTile;
+    } else if (cta == 0) {
+      report_error(a.error, TLA_ERR_POSITION);
+    }
+    prefix[b + 1] = tiles * Hk;
+  }
+  if (tid == 0) {
+    prefix[0] = 0;
+    flags[0] = 0;
+    flags[1] = 0;
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 0) {  // inclusive scan of prefix[1..batch]
+    int carry = 0;
+    for (int base = 1; base <= p.batch; base += 32) {
+      const int i = base + lane;
+      int v = i <= p.batch ? prefix[i] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      if (i <= p.batch) prefix[i] = v + carry;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+  const long long total = prefix[p.batch];
+
+  // Sequence-shard mode: pairs with no local tokens still emit an empty triple.
+  if (p.partial_out != nullptr) {
+    for (int b = cta; b < p.batch; b += grid) {
+      if (prefix[b + 1] != prefix[b]) continue;
+      for (int i = tid; i < Hq * (D + 2); i += kThreads) {
+        const int h = i / (D + 2), e = i - h * (D + 2);
+        p.partial_out[(static_cast<size_t>(b) * Hq + h) * (D + 2) + e] = e == 0 ? -INFINITY : 0.f;
+      }
+    }
+  }
+  if (total == 0) return;
+  const long long tb = cta_begin(cta, total, grid);
+  const long long te = cta_begin(cta + 1, total, grid);
+  if (tb >= te) return;
+
+  uint8_t* stages = smem + L.stages;
+
+  if (warp == kConsumerWarps) {
+    // ================================================================ producer
+    if (lane == 0) {
+      tma_prefetch(&p.tmap_k);
+      tma_prefetch(&p.tmap_v);
+      uint32_t it = 0;
+      int b = 0;
+      for (long long g = tb; g < te;) {
+        while (prefix[b + 1] <= g) ++b;
+        const int tiles = (prefix[b + 1] - prefix[b]) / Hk;
+        const int off = static_cast<int>(g - prefix[b]);
+        const int kvh = off / tiles, lt = off - kvh * tiles;
+        const int n = static_cast<int>(min(te - g, static_cast<long long>(tiles - lt)));
+        int lo, hi;
+        seq_range(a, p.positions[b], p.slot_offset, p.local_tokens, &lo, &hi);
+        for (int j = lt; j < lt + n; ++j, ++it) {
+          const int s = it % C::kStages;
+          const uint32_t ph = (it / C::kStages) & 1u;
+          if (flags[0] || !mbar_wait(&empty[s], ph ^ 1u, a.error)) {
+            flags[0] = 1;
+            continue;
+          }
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          uint8_t* kst = stages + s * C::kStageBytes;
+          const int y = lo + j * kTile, z = b * Hk + kvh;
+#pragma unroll
+          for (int x = 0; x < C::kBoxes; ++x) {
+            tma_load_3d(kst + x * C::kBoxBytes, &p.tmap_k, &full[s], x * 64, y, z);
+            tma_load_3d(kst + C::kTileBytes + x * C::kBoxBytes, &p.tmap_v, &full[s], x * 64, y, z);
+          }
+        }
+        g += n;
+      }
+      // Do not leave the CTA with copies in flight: the last stages' loads
+      // have landed once their full barriers completed.
+      const uint32_t first = it > static_cast<uint32_t>(C::kStages) ? it - C::kStages : 0u;
+      for (uint32_t i = first; i < it; ++i)
+        if (!flags[0]) mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1u, a.error);
+    }
+    return;
+  }
+
+  // ================================================================== consumers
+  const IO* qkv = static_cast<const IO*>(p.qkv);
+  __half* q_s = reinterpret_cast<__half*>(smem + L.q);
+  float* qf = reinterpret_cast<float*>(smem + L.qf);
+  float* kvf = reinterpret_cast<float*>(smem + L.kvf);
+  float* cs = reinterpret_cast<float*>(smem + L.cs);
+  __half* newkv = reinterpret_cast<__half*>(smem + L.newkv);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  const int half = a.rotary / 2;
+  const float scale = a.attn_scale * kLog2e;
+  const int g_row = lane >> 2, t4 = lane & 3;
+  const int row_stride = (Hq + 2 * Hk) * D;
+  uint32_t it = 0;
+  int b = 0;
+
+  for (long long g = tb; g < te;) {
+    while (prefix[b + 1] <= g) ++b;
+    const int tiles = (prefix[b + 1] - prefix[b]) / Hk;
+    const int off = static_cast<int>(g - prefix[b]);
+    const int kvh = off / tiles, lt = off - kvh * tiles;
+    const int n = static_cast<int>(min(te - g, static_cast<long long>(tiles - lt)));
+    const int pos = p.positions[b];
+    int lo, hi;
+    seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
+    const int slot_new = pos - p.slot_offset;
+    const bool has_new = p.append && (lt + n == tiles);
+    const IO* row = qkv + static_cast<size_t>(b) * row_stride;
+
+    // ---- segment setup: QK-norm + RoPE of the group's queries (and the new K/V)
+    for (int i = tid; i < G * D; i += 128) qf[i] = to_f32(row[kvh * G * D + i]);
+    if (has_new)
+      for (int i = tid; i < D; i += 128) {
+        kvf[i] = to_f32(row[(Hq + kvh) * D + i]);
+        kvf[D + i] = to_f32(row[(Hq + Hk + kvh) * D + i]);
+      }
+    for (int j = tid; j < half; j += 128) {
+      float c = 1.f, s = 0.f;
+      if (j < a.pair_count) rope_cos_sin(pos, a.inv_freq[j], &c, &s);
+      cs[j] = c;
+      cs[D / 2 + j] = s;
+    }
+    named_barrier_sync(1, 128);
+    for (int h = warp; h < G + 2; h += kConsumerWarps) {  // per-head RMS norms, math.ts:154-167
+      const float* w;
+      float* v;
+      if (h < G) {
+        if (a.q_norm == nullptr) continue;
+        w = a.q_norm;
+        v = qf + h * D;
+      } else if (h == G) {
+        if (!has_new || a.k_norm == nullptr) continue;
+        w = a.k_norm;
+        v = kvf;
+      } else {
+        if (!has_new || !a.v_norm) continue;
+        w = nullptr;
+        v = kvf + D;
+      }
+      float ss = 0.f;
+      for (int d = lane; d < D; d += 32) ss += v[d] * v[d];
+      ss = warp_sum(ss);
+      const float inv_rms = 1.f / sqrtf(ss / static_cast<float>(D) + a.rms_eps);
+      __syncwarp();
+      for (int d = lane; d < D; d += 32) {
+        const float sc = w == nullptr ? 1.f : (a.offset_rms ? 1.f + w[d] : w[d]);
+        v[d] = v[d] * inv_rms * sc;
+      }
+    }
+    named_barrier_sync(1, 128);
+    auto rope = [&](const float* v, int d) -> float {
+      float val = v[d];
+      if (d < a.rotary) {
+        const int j = d < half ? d : d - half;
+        if (j < a.pair_count) {
+          const float partner = d < half ? -v[d + half] : v[d - half];
+          val = (val * cs[j] + partner * cs[D / 2 + j]) * a.attn_factor;
+        }
+      }
+      return val;
+    };
+    for (int i = tid; i < 16 * D; i += 128) {
+      const int r = i / D, d = i - r * D;
+      q_s[r * (C::kQPitch / 2) + d] = __float2half_rn(r < G ? rope(qf + r * D, d) : 0.f);
+    }
+    if (has_new)
+      for (int d = tid; d < D; d += 128) {
+        newkv[d] = __float2half_rn(rope(kvf, d));
+        newkv[D + d] = __float2half_rn(kvf[D + d]);
+      }
+    named_barrier_sync(1, 128);
+    if (has_new && tid < D / 8) {  // append to the cache (copy-KV, TSLAttention.ts:280-281)
+      const size_t base = ((static_cast<size_t>(b) * Hk + kvh) * a.max_tokens + slot_new) * D + tid * 8;
+      reinterpret_cast<uint4*>(static_cast<__half*>(a.k_cache) + base)[0] = reinterpret_cast<const uint4*>(newkv)[tid];
+      reinterpret_cast<uint4*>(static_cast<__half*>(a.v_cache) + base)[0] =
+          reinterpret_cast<const uint4*>(newkv + D)[tid];
+    }
+    uint32_t qa[D / 16][4];
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int ch = 2 * kk + (lane >> 4);
+      ldsm_x4(smem_u32(q_s) + r * C::kQPitch + ch * 16, qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+    }
+
+    float o[D / 8][4];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    // ---- stream the segment's tiles
+    for (int j = lt; j < lt + n; ++j, ++it) {
+      const int s = it % C::kStages;
+      const uint32_t ph = (it / C::kStages) & 1u;
+      if (!flags[0] && !mbar_wait(&full[s], ph, a.error)) flags[0] = 1;
+      uint8_t* kst = stages + s * C::kStageBytes;
+      uint8_t* vst = kst + C::kTileBytes;
+      const int y0 = lo + j * kTile;
+      const int tok0 = warp * 16;
+      bool wrote = false;
+      if (has_new && j == tiles - 1) {  // the new token's row holds the fresh K/V
+        const int r = slot_new - y0;
+        if (r >= tok0 && r < tok0 + 16 && lane < D / 8) {
+          const int box = lane >> 3, ch = lane & 7;
+          *reinterpret_cast<uint4*>(kst + box * C::kBoxBytes + sw128(r, ch)) =
+              reinterpret_cast<const uint4*>(newkv)[lane];
+          *reinterpret_cast<uint4*>(vst + box * C::kBoxBytes + sw128(r, ch)) =
+              reinterpret_cast<const uint4*>(newkv + D)[lane];
+          wrote = true;
+        }
+        __syncwarp();
+      }
+      // S = Q K^T over this warp's 16 tokens
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      const uint32_t kbase = smem_u32(kst);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int tok = tok0 + (lane & 7) + ((lane >> 4) << 3);
+        const int chunk = 2 * kk + ((lane >> 3) & 1);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(kbase + (chunk >> 3) * C::kBoxBytes + sw128(tok, chunk & 7), r0, r1, r2, r3);
+        mma_16816(acc[0], qa[kk], r0, r1);
+        mma_16816(acc[1], qa[kk], r2, r3);
+      }
+      // mask + online softmax (log2 domain)
+      float x[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = y0 + tok0 + nt * 8 + 2 * t4 + (e & 1);
+          x[nt][e] = tok <= hi ? acc[nt][e] * scale : -INFINITY;
+        }
+      float mt0 = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
+      mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, 1));
+      mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, 2));
+      const float mn0 = fmaxf(m0, mt0);
+      const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
+      const float al0 = ex2(m0 - mu0);
+      m0 = mn0;
+      float pr[2][4];
+      pr[0][0] = ex2(x[0][0] - mu0);
+      pr[0][1] = ex2(x[0][1] - mu0);
+      pr[1][0] = ex2(x[1][0] - mu0);
+      pr[1][1] = ex2(x[1][1] - mu0);
+      l0 = l0 * al0 + (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+      float al1 = 1.f;
+      if (TWO_ROWS) {
+        float mt1 = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
+        mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, 1));
+        mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, 2));
+        const float mn1 = fmaxf(m1, mt1);
+        const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
+        al1 = ex2(m1 - mu1);
+        m1 = mn1;
+        pr[0][2] = ex2(x[0][2] - mu1);
+        pr[0][3] = ex2(x[0][3] - mu1);
+        pr[1][2] = ex2(x[1][2] - mu1);
+        pr[1][3] = ex2(x[1][3] - mu1);
+        l1 = l1 * al1 + (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+      }
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][0] *= al0;
+        o[i][1] *= al0;
+        if (TWO_ROWS) {
+          o[i][2] *= al1;
+          o[i][3] *= al1;
+        }
+      }
+      uint32_t pa[4];
+      pa[0] = pack_half2(pr[0][0], pr[0][1]);
+      pa[1] = TWO_ROWS ? pack_half2(pr[0][2], pr[0][3]) : 0u;
+      pa[2] = pack_half2(pr[1][0], pr[1][1]);
+      pa[3] = TWO_ROWS ? pack_half2(pr[1][2], pr[1][3]) : 0u;
+      // O += P V
+      const uint32_t vbase = smem_u32(vst);
+#pragma unroll
+      for (int dd = 0; dd < D / 16; ++dd) {
+        const int tok = tok0 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int chunk = 2 * dd + (lane >> 4);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(vbase + (chunk >> 3) * C::kBoxBytes + sw128(tok, chunk & 7), r0, r1, r2, r3);
+        mma_16816(o[2 * dd], pa, r0, r1);
+        mma_16816(o[2 * dd + 1], pa, r2, r3);
+      }
+      if (wrote) fence_proxy_async_smem();  // generic writes before the next TMA into this stage
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ---- merge the 4 warps' (m, l, O)
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    if (TWO_ROWS) {
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    }
+    float* rw = red + warp * G * (D + 2);
+    if (g_row < G) {
+      float* rr = rw + g_row * (D + 2);
+      if (t4 == 0) {
+        rr[0] = m0;
+        rr[1] = l0;
+      }
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        rr[2 + i * 8 + 2 * t4] = o[i][0];
+        rr[2 + i * 8 + 2 * t4 + 1] = o[i][1];
+      }
+    }
+    if (TWO_ROWS && g_row + 8 < G) {
+      float* rr = rw + (g_row + 8) * (D + 2);
+      if (t4 == 0) {
+        rr[0] = m1;
+        rr[1] = l1;
+      }
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        rr[2 + i * 8 + 2 * t4] = o[i][2];
+        rr[2 + i * 8 + 2 * t4 + 1] = o[i][3];
+      }
+    }
+    named_barrier_sync(1, 128);
+    const bool whole = (lt == 0 && n == tiles);
+    const int slot = (g == tb) ? 0 : 1;
+    float* mine = p.scratch + (static_cast<size_t>(cta) * 2 + slot) * G * (D + 2);
+    for (int i = tid; i < G * (D + 2); i += 128) {
+      const int r = i / (D + 2), e = i - r * (D + 2);
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, red[(w * G + r) * (D + 2)]);
+      float v = 0.f;
+      if (e == 0) {
+        v = M;
+      } else if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float* rr = red + (w * G + r) * (D + 2);
+          v += rr[e] * ex2(rr[0] - M);
+        }
+      }
+      if (!whole) {
+        mine[i] = v;
+      } else if (p.partial_out) {
+        p.partial_out[(static_cast<size_t>(b) * Hq + kvh * G + r) * (D + 2) + e] = v;
+      } else if (e >= 2) {
+        // out = O / l (x sigmoid(gate)); l is red-combined in the e == 1 slot
+        float Lsum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float* rr = red + (w * G + r) * (D + 2);
+          Lsum += rr[1] * ex2(rr[0] - M);
+        }
+        float val = v / Lsum;
+        const size_t oi = (static_cast<size_t>(b) * Hq + kvh * G + r) * D + (e - 2);
+        if (p.gate) val = val * (1.f / (1.f + expf(-to_f32(static_cast<const IO*>(p.gate)[oi]))));
+        static_cast<IO*>(p.out)[oi] = from_f32<IO>(val);
+      }
+    }
+    if (!whole) {
+      // ---- ticket: the CTA that completes the pair merges all its segments
+      __threadfence();
+      named_barrier_sync(1, 128);
+      const int pair = b * Hk + kvh;
+      if (tid == 0) {
+        const int old = atomicAdd(&p.counters[pair], n);
+        flags[1] = (old + n == tiles) ? 1 : 0;
+      }
+      named_barrier_sync(1, 128);
+      if (flags[1]) {
+        __threadfence();
+        const long long pb = prefix[b] + static_cast<long long>(kvh) * tiles;
+        const int c0 = cta_of(pb, total, grid), c1 = cta_of(pb + tiles - 1, total, grid);
+        for (int i = tid; i < G * (D + 2); i += 128) {
+          const int r = i / (D + 2), e = i - r * (D + 2);
+          float M = -INFINITY;
+          for (int c = c0; c <= c1; ++c) {
+            const int sl = cta_begin(c, total, grid) >= pb ? 0 : 1;
+            M = fmaxf(M, __ldcg(p.scratch + ((static_cast<size_t>(c) * 2 + sl) * G + r) * (D + 2)));
+          }
+          float v = 0.f, Lsum = 0.f;
+          for (int c = c0; c <= c1; ++c) {
+            const int sl = cta_begin(c, total, grid) >= pb ? 0 : 1;
+            const float* pc = p.scratch + ((static_cast<size_t>(c) * 2 + sl) * G + r) * (D + 2);
+            const float w = ex2(__ldcg(pc) - M);
+            if (e >= 1) v += __ldcg(pc + e) * w;
+            if (e >= 2 && !p.partial_out) Lsum += __ldcg(pc + 1) * w;
+          }
+          if (e == 0) v = M;
+          if (p.partial_out) {
+            p.partial_out[(static_cast<size_t>(b) * Hq + kvh * G + r) * (D + 2) + e] = v;
+          } else if (e >= 2) {
+            float val = v / Lsum;
+            const size_t oi = (static_cast<size_t>(b) * Hq + kvh * G + r) * D + (e - 2);
+            if (p.gate) val = val * (1.f / (1.f + expf(-to_f32(static_cast<const IO*>(p.gate)[oi]))));
+            static_cast<IO*>(p.out)[oi] = from_f32<IO>(val);
+          }
+        }
+        if (tid == 0) p.counters[pair] = 0;
+      }
+    }
+    named_barrier_sync(1, 128);  // red / q_s / flags reuse by the next segment
+    g += n;
+  }
+}
+
+template <int D, typename IO, bool TWO>
+cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, cudaStream_t stream) {
+  const SmemLayout s = smem_layout<D>(L->G, p.batch);
+  decode_fast_kernel<D, IO, TWO><<<L->decode_grid, kThreads, s.total, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <int D, typename IO, bool TWO>
+cudaError_t configure_t(tla_layer* L, int* blocks) {
+  const SmemLayout s = smem_layout<D>(L->G, L->max_batch);
+  auto k = decode_fast_kernel<D, IO, TWO>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, s.total);
+  if (e != cudaSuccess) return e;
+  L->decode_smem = s.total;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k, kThreads, s.total);
+}
+
+template <int D>
+cudaError_t dispatch_configure(tla_layer* L, int* blocks) {
+  const bool two = L->G > 8;
+  if (L->io_fp32) return two ? configure_t<D, float, true>(L, blocks) : configure_t<D, float, false>(L, blocks);
+  return two ? configure_t<D, __half, true>(L, blocks) : configure_t<D, __half, false>(L, blocks);
+}
+
+template <int D>
+cudaError_t dispatch_launch(const tla_layer* L, const DecodeParams& p, cudaStream_t stream) {
+  const bool two = L->G > 8;
+  if (L->io_fp32) return two ? launch_t<D, float, true>(L, p, stream) : launch_t<D, float, false>(L, p, stream);
+  return two ? launch_t<D, __half, true>(L, p, stream) : launch_t<D, __half, false>(L, p, stream);
+}
+
+CUresult make_cache_map(const tla_layer* L, void* base, CUtensorMap* map) {
+  // 3-D view of the cache: x = head_dim (contiguous), y = token slot, z = (sequence, kv head)
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(L->D), static_cast<cuuint64_t>(L->max_tokens),
+                              static_cast<cuuint64_t>(L->max_batch) * L->Hk};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(L->D) * 2,
+                                 static_cast<cuuint64_t>(L->D) * 2 * L->max_tokens};
+  const cuuint32_t box[3] = {64, kTile, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return L->ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace
+
+cudaError_t decode_fast_configure(tla_layer* L) {
+  L->fast_decode = false;
+  if (L->cache_fp32 || (L->D != 64 && L->D != 128) || L->Hq % L->Hk != 0 || L->G > 16 ||
+      L->max_batch > kMaxBatch || L->ctx->encode_tiled == nullptr)
+    return cudaSuccess;
+  if (make_cache_map(L, L->k_cache, &L->tmap_k) != CUDA_SUCCESS ||
+      make_cache_map(L, L->v_cache, &L->tmap_v) != CUDA_SUCCESS)
+    return cudaSuccess;  // fall back to the generic path
+  int blocks = 0;
+  cudaError_t e = L->D == 64 ? dispatch_configure<64>(L, &blocks) : dispatch_configure<128>(L, &blocks);
+  if (e != cudaSuccess) return e;
+  if (blocks <= 0) return cudaSuccess;
+  L->decode_grid = blocks * L->ctx->sm_count;
+  L->fast_decode = true;
+  return cudaSuccess;
+}
+
+size_t decode_fast_scratch_floats(const tla_layer* L) {
+  return static_cast<size_t>(L->decode_grid) * 2 * L->G * (L->D + 2);
+}
+
+cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_t* positions, const void* gate,
+                               void* out, float* partial, int batch, int slot_offset, int local_tokens, int append,
+                               cudaStream_t stream) {
+  DecodeParams p;
+  p.tmap_k = L->tmap_k;
+  p.tmap_v = L->tmap_v;
+  p.a = layer_args(L);
+  p.qkv = qkv;
+  p.positions = positions;
+  p.gate = gate;
+  p.out = out;
+  p.partial_out = partial;
+  p.scratch = L->ctx->d_partials;
+  p.counters = L->ctx->d_counters;
+  p.batch = batch;
+  p.slot_offset = slot_offset;
+  p.local_tokens = local_tokens;
+  p.append = append;
+  return L->D == 64 ? dispatch_launch<64>(L, p, stream) : dispatch_launch<128>(L, p, stream);
+}
+
+}  // namespace tla

@@ -1,0 +1,304 @@
+// Generic attention path: any head_dim <= 256, any GQA ratio, fp16 or fp32
+// cache. Used for shapes the tensor-core kernels do not cover (the reference's
+// own test shapes use head_dim 2, 4 and 8) and for float32 caches.
+//
+// rope_append_kernel  <- TSLAttention copy-KV and query kernels
+//                        (packages/three-llm/src/tsl/TSLAttention.ts:252-304)
+//                        and causalAttention's QK-norm / RoPE / append steps
+//                        (packages/three-llm/src/runtime/math.ts:211-238)
+// attend_generic_kernel <- scores + softmax/PV kernels (TSLAttention.ts:306-428),
+//                        math.ts:242-273, as a single online-softmax pass.
+#include <math.h>
+
+#include "tla_device.cuh"
+#include "tla_internal.h"
+
+namespace tla {
+
+namespace {
+
+constexpr int kThreads = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float block_reduce_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  v = red[0];
+#pragma unroll
+  for (int i = 1; i < kThreads / 32; ++i) v = fmaxf(v, red[i]);
+  return v;
+}
+
+__device__ __forceinline__ float block_reduce_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  v = 0.f;
+#pragma unroll
+  for (int i = 0; i < kThreads / 32; ++i) v += red[i];
+  return v;
+}
+
+// One block per (t, b) token row of qkv.
+template <typename IO, typename CT>
+__global__ void __launch_bounds__(kThreads) rope_append_kernel(LayerArgs a, const IO* __restrict__ qkv,
+                                                               const int32_t* __restrict__ start, int seq_len,
+                                                               int slot_offset, int append, float* __restrict__ qscr) {
+  extern __shared__ float smem[];
+  const int t = blockIdx.x, b = blockIdx.y;
+  const int D = a.D, Hq = a.Hq, Hk = a.Hk;
+  const int heads = Hq + 2 * Hk;
+  const int pos = start[b] + t;
+  const int slot = pos - slot_offset;
+  if (pos < 0 || (append && (slot < 0 || slot >= a.max_tokens))) {
+    if (threadIdx.x == 0) report_error(a.error, TLA_ERR_POSITION);
+    return;
+  }
+  float* x = smem;                       // [heads * D]
+  float* cs = smem + heads * D;          // [rotary/2] cos
+  float* sn = cs + (a.rotary / 2 + 1);   // [rotary/2] sin
+  float* red = sn + (a.rotary / 2 + 1);  // [4]
+  (void)red;
+  const IO* row = qkv + (static_cast<size_t>(b) * seq_len + t) * heads * D;
+  const int nload = (append ? heads : Hq) * D;
+  for (int i = threadIdx.x; i < nload; i += kThreads) x[i] = to_f32(row[i]);
+  const int half = a.rotary / 2;
+  for (int j = threadIdx.x; j < half; j += kThreads) {
+    float c = 1.f, s = 0.f;
+    if (j < a.pair_count) rope_cos_sin(pos, a.inv_freq[j], &c, &s);
+    cs[j] = c;
+    sn[j] = s;
+  }
+  __syncthreads();
+  // Per-head RMS norms (math.ts:78-97 / :154-167): one warp per head.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int norm_heads = append ? heads : Hq;
+  for (int h = warp; h < norm_heads; h += kThreads / 32) {
+    const float* w = nullptr;
+    bool on = false;
+    if (h < Hq) {
+      w = a.q_norm;
+      on = w != nullptr;
+    } else if (h < Hq + Hk) {
+      w = a.k_norm;
+      on = w != nullptr;
+    } else {
+      on = a.v_norm != 0;  // weightless
+    }
+    if (!on) continue;
+    float* v = x + h * D;
+    float ss = 0.f;
+    for (int d = lane; d < D; d += 32) ss += v[d] * v[d];
+    ss = warp_sum(ss);
+    const float inv_rms = 1.f / sqrtf(ss / static_cast<float>(D) + a.rms_eps);
+    __syncwarp();
+    for (int d = lane; d < D; d += 32) {
+      const float scale = w == nullptr ? 1.f : (a.offset_rms ? 1.f + w[d] : w[d]);
+      v[d] = v[d] * inv_rms * scale;
+    }
+  }
+  __syncthreads();
+  // RoPE, rotate-half layout (math.ts:134-147) and the stores.
+  const int rope_heads = append ? Hq + Hk : Hq;
+  for (int i = threadIdx.x; i < rope_heads * D; i += kThreads) {
+    const int h = i / D, d = i - h * D;
+    const float* v = x + h * D;
+    float val = v[d];
+    if (half > 0 && d < a.rotary) {
+      const int j = d < half ? d : d - half;
+      if (j < a.pair_count) {
+        const float partner = d < half ? -v[d + half] : v[d - half];
+        val = (val * cs[j] + partner * sn[j]) * a.attn_factor;
+      }
+    }
+    if (h < Hq) {
+      qscr[((static_cast<size_t>(b) * seq_len + t) * Hq + h) * D + d] = val;
+    } else {
+      const int kh = h - Hq;
+      CT* kc = static_cast<CT*>(a.k_cache);
+      kc[((static_cast<size_t>(b) * Hk + kh) * a.max_tokens + slot) * D + d] = from_f32<CT>(val);
+    }
+  }
+  if (append) {
+    CT* vc = static_cast<CT*>(a.v_cache);
+    for (int i = threadIdx.x; i < Hk * D; i += kThreads) {
+      const int kh = i / D, d = i - kh * D;
+      vc[((static_cast<size_t>(b) * Hk + kh) * a.max_tokens + slot) * D + d] =
+          from_f32<CT>(x[(Hq + Hk + kh) * D + d]);
+    }
+  }
+}
+
+// One block per (h, t, b) query; online softmax over 128-token chunks.
+template <typename CT, typename IO>
+__global__ void __launch_bounds__(kThreads)
+    attend_generic_kernel(LayerArgs a, const float* __restrict__ qscr, const int32_t* __restrict__ start, int seq_len,
+                          int slot_offset, int local_tokens, const IO* __restrict__ gate, IO* __restrict__ out,
+                          float* __restrict__ partial) {
+  extern __shared__ float smem[];
+  const int h = blockIdx.x, t = blockIdx.y, b = blockIdx.z;
+  const int D = a.D, Hq = a.Hq, Hk = a.Hk;
+  const int pos = start[b] + t;
+  if (pos < 0) return;  // reported by rope_append_kernel
+  float* q = smem;            // [D]
+  float* o = q + D;           // [D]
+  float* p = o + D;           // [kThreads]
+  float* red = p + kThreads;  // [4]
+  const int kvh = static_cast<int>((static_cast<long long>(h) * Hk) / Hq);  // TSLAttention.ts:340
+  const size_t qrow = (static_cast<size_t>(b) * seq_len + t) * Hq + h;
+  for (int d = threadIdx.x; d < D; d += kThreads) {
+    q[d] = qscr[qrow * D + d];
+    o[d] = 0.f;
+  }
+  const int first = a.sliding > 0 ? max(0, pos - a.sliding + 1) : 0;  // math.ts:208
+  const int lo = max(first, slot_offset) - slot_offset;
+  const int hi = min(pos, slot_offset + local_tokens - 1) - slot_offset;
+  const CT* kc = static_cast<const CT*>(a.k_cache) + (static_cast<size_t>(b) * Hk + kvh) * a.max_tokens * D;
+  const CT* vc = static_cast<const CT*>(a.v_cache) + (static_cast<size_t>(b) * Hk + kvh) * a.max_tokens * D;
+  const float scale = a.attn_scale * kLog2e;
+  float m = -INFINITY, l = 0.f;
+  __syncthreads();
+  for (int c = lo; c <= hi; c += kThreads) {
+    const int tok = c + threadIdx.x;
+    float s = -INFINITY;
+    if (tok <= hi) {
+      const CT* kr = kc + static_cast<size_t>(tok) * D;
+      float dot = 0.f;
+      for (int d = 0; d < D; ++d) dot += q[d] * to_f32(kr[d]);
+      s = dot * scale;
+    }
+    const float m_new = fmaxf(m, block_reduce_max(s, red));
+    const float alpha = ex2(m - m_new);
+    const float pv = tok <= hi ? ex2(s - m_new) : 0.f;
+    p[threadIdx.x] = pv;
+    l = l * alpha + block_reduce_sum(pv, red);
+    const int n = min(kThreads, hi - c + 1);
+    for (int d = threadIdx.x; d < D; d += kThreads) {
+      float acc = o[d] * alpha;
+      const CT* vr = vc + static_cast<size_t>(c) * D + d;
+      for (int j = 0; j < n; ++j) acc += p[j] * to_f32(vr[static_cast<size_t>(j) * D]);
+      o[d] = acc;
+    }
+    m = m_new;
+    __syncthreads();
+  }
+  if (partial) {
+    float* pr = partial + qrow * (D + 2);
+    if (threadIdx.x == 0) {
+      pr[0] = m;
+      pr[1] = l;
+    }
+    for (int d = threadIdx.x; d < D; d += kThreads) pr[2 + d] = o[d];
+    return;
+  }
+  const float inv_l = l > 0.f ? 1.f / l : 0.f;
+  for (int d = threadIdx.x; d < D; d += kThreads) {
+    float v = o[d] * inv_l;
+    if (gate) v = v * (1.f / (1.f + expf(-to_f32(gate[qrow * D + d]))));  // math.ts:271-273
+    out[qrow * D + d] = from_f32<IO>(v);
+  }
+}
+
+template <typename IO, typename CT>
+cudaError_t rope_append_t(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
+                          int slot_offset, int append, float* qscr, cudaStream_t stream) {
+  const LayerArgs a = layer_args(L);
+  const size_t smem = sizeof(float) * (static_cast<size_t>(L->Hq + 2 * L->Hk) * L->D + 2 * (L->rotary / 2 + 1) + 4);
+  auto k = rope_append_kernel<IO, CT>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  k<<<dim3(seq_len, batch), kThreads, smem, stream>>>(a, static_cast<const IO*>(qkv), start, seq_len, slot_offset,
+                                                      append, qscr);
+  return cudaGetLastError();
+}
+
+template <typename CT, typename IO>
+cudaError_t attend_t(const tla_layer* L, const float* qscr, const int32_t* start, int batch, int seq_len,
+                     int slot_offset, int local_tokens, const void* gate, void* out, float* partial,
+                     cudaStream_t stream) {
+  const LayerArgs a = layer_args(L);
+  const size_t smem = sizeof(float) * (2 * static_cast<size_t>(L->D) + kThreads + 4);
+  attend_generic_kernel<CT, IO><<<dim3(L->Hq, seq_len, batch), kThreads, smem, stream>>>(
+      a, qscr, start, seq_len, slot_offset, local_tokens, static_cast<const IO*>(gate), static_cast<IO*>(out),
+      partial);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_rope_append(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
+                               int slot_offset, int append, float* qscr, cudaStream_t stream) {
+  if (L->io_fp32)
+    return L->cache_fp32 ? rope_append_t<float, float>(L, qkv, start, batch, seq_len, slot_offset, append, qscr, stream)
+                         : rope_append_t<float, __half>(L, qkv, start, batch, seq_len, slot_offset, append, qscr, stream);
+  return L->cache_fp32 ? rope_append_t<__half, float>(L, qkv, start, batch, seq_len, slot_offset, append, qscr, stream)
+                       : rope_append_t<__half, __half>(L, qkv, start, batch, seq_len, slot_offset, append, qscr, stream);
+}
+
+cudaError_t launch_attend_generic(const tla_layer* L, const float* qscr, const int32_t* start, int batch,
+                                  int seq_len, int slot_offset, int local_tokens, const void* gate, void* out,
+                                  float* partial, cudaStream_t stream) {
+  if (L->io_fp32)
+    return L->cache_fp32
+               ? attend_t<float, float>(L, qscr, start, batch, seq_len, slot_offset, local_tokens, gate, out, partial,
+                                        stream)
+               : attend_t<__half, float>(L, qscr, start, batch, seq_len, slot_offset, local_tokens, gate, out, partial,
+                                         stream);
+  return L->cache_fp32
+             ? attend_t<float, __half>(L, qscr, start, batch, seq_len, slot_offset, local_tokens, gate, out, partial,
+                                       stream)
+             : attend_t<__half, __half>(L, qscr, start, batch, seq_len, slot_offset, local_tokens, gate, out, partial,
+                                        stream);
+}
+
+// ---------------------------------------------------------------- LSE combine
+namespace {
+template <typename IO>
+__global__ void combine_lse_kernel(const float* __restrict__ partials, int ranks, int rows, int D,
+                                   const IO* __restrict__ gate, IO* __restrict__ out) {
+  const int row = blockIdx.x;  // (b, h)
+  const size_t stride = static_cast<size_t>(rows) * (D + 2);
+  float M = -INFINITY;
+  for (int r = 0; r < ranks; ++r) M = fmaxf(M, partials[r * stride + static_cast<size_t>(row) * (D + 2)]);
+  float Lsum = 0.f;
+  for (int r = 0; r < ranks; ++r) {
+    const float* p = partials + r * stride + static_cast<size_t>(row) * (D + 2);
+    Lsum += p[1] * ex2(p[0] - M);
+  }
+  const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < ranks; ++r) {
+      const float* p = partials + r * stride + static_cast<size_t>(row) * (D + 2);
+      acc += p[2 + d] * ex2(p[0] - M);
+    }
+    float v = acc * inv;
+    if (gate) v = v * (1.f / (1.f + expf(-to_f32(gate[static_cast<size_t>(row) * D + d]))));
+    out[static_cast<size_t>(row) * D + d] = from_f32<IO>(v);
+  }
+}
+}  // namespace
+
+cudaError_t launch_combine_lse(const float* partials, int ranks, int batch, int Hq, int D, const void* gate,
+                               void* out, bool io_fp32, cudaStream_t stream) {
+  const int rows = batch * Hq;
+  if (rows == 0) return cudaSuccess;
+  const int threads = D >= 128 ? 128 : (D >= 64 ? 64 : 32);
+  if (io_fp32)
+    combine_lse_kernel<float><<<rows, threads, 0, stream>>>(partials, ranks, rows, D, static_cast<const float*>(gate),
+                                                            static_cast<float*>(out));
+  else
+    combine_lse_kernel<__half><<<rows, threads, 0, stream>>>(partials, ranks, rows, D,
+                                                             static_cast<const __half*>(gate), static_cast<__half*>(out));
+  return cudaGetLastError();
+}
+
+}  // namespace tla

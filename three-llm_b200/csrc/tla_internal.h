@@ -1,0 +1,94 @@
+// Host-side state and kernel entry points shared by the translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include "tla_api.h"
+
+struct tla_ctx {
+  int device = 0;
+  int sm_count = 0;
+  int* d_error = nullptr;  // sticky device error word (first error wins)
+  // split-KV scratch: partial triples of the persistent decode kernel and the
+  // per-(sequence, kv head) completion counters (zero between launches)
+  float* d_partials = nullptr;
+  size_t partial_floats = 0;
+  int32_t* d_counters = nullptr;
+  size_t counter_count = 0;
+  // prefill / generic-path query scratch (rotated queries)
+  void* d_qscratch = nullptr;
+  size_t qscratch_bytes = 0;
+  PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
+};
+
+struct tla_layer {
+  tla_ctx* ctx = nullptr;
+  tla_attn_config cfg{};
+  int Hq = 0, Hk = 0, D = 0, G = 0;
+  int max_tokens = 0, max_batch = 0;
+  int rotary = 0, freq_half = 0, pair_count = 0, sliding = 0;
+  float attn_scale = 0.f, attn_factor = 1.f, rms_eps = 1e-6f;
+  bool io_fp32 = false, cache_fp32 = false, v_norm = false, offset_rms = false;
+  bool has_qnorm = false, has_knorm = false;
+  bool borrowed = false;        // sharedAttention: cache belongs to another layer
+  void* k_cache = nullptr;
+  void* v_cache = nullptr;
+  float* d_inv_freq = nullptr;  // [max(freq_half, 1)]
+  float* d_qnorm = nullptr;     // [D] or null
+  float* d_knorm = nullptr;     // [D] or null
+  // fast decode path (fp16 cache, D in {64, 128}, G <= 16)
+  bool fast_decode = false;
+  int decode_grid = 0;          // persistent CTAs per launch
+  size_t decode_smem = 0;
+  CUtensorMap tmap_k{}, tmap_v{};
+  // tensor-core prefill path
+  bool fast_prefill = false;
+};
+
+namespace tla {
+
+// Parameters shared by all decode / prefill kernels of one layer.
+struct LayerArgs {
+  void* k_cache;
+  void* v_cache;
+  const float* inv_freq;
+  const float* q_norm;  // null => none
+  const float* k_norm;  // null => none
+  int* error;
+  int Hq, Hk, D, G;
+  int max_tokens;
+  int rotary, freq_half, pair_count, sliding;
+  float attn_scale, attn_factor, rms_eps;
+  int v_norm, offset_rms;
+};
+
+LayerArgs layer_args(const tla_layer* L);
+
+// Generic path (any head_dim <= 256, any GQA ratio, fp16 or fp32 cache).
+// rope_append: per (b, t) token at pos = start[b] + t: QK-norm + RoPE of Q into
+// qscr (float32 [B][S][Hq][D]); if append, K (norm + RoPE) and V (vNorm) into
+// cache slot pos - slot_offset.
+cudaError_t launch_rope_append(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
+                               int slot_offset, int append, float* qscr, cudaStream_t stream);
+// attend: output or partial triples for each (b, t, h) query over cache slots
+// [max(window start, slot_offset), min(pos, slot_offset + local_tokens - 1)] - slot_offset.
+cudaError_t launch_attend_generic(const tla_layer* L, const float* qscr, const int32_t* start, int batch,
+                                  int seq_len, int slot_offset, int local_tokens, const void* gate, void* out,
+                                  float* partial, cudaStream_t stream);
+// Fast persistent split-KV decode (TMA + tensor-core tiles); partial != null
+// switches to partial-triple output (sequence sharding).
+cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_t* positions, const void* gate,
+                               void* out, float* partial, int batch, int slot_offset, int local_tokens, int append,
+                               cudaStream_t stream);
+cudaError_t decode_fast_configure(tla_layer* L);
+cudaError_t launch_combine_lse(const float* partials, int ranks, int batch, int Hq, int D, const void* gate,
+                               void* out, bool io_fp32, cudaStream_t stream);
+// Tensor-core prefill (tcgen05/TMEM/TMA), fp16 cache, D in {64, 128}.
+cudaError_t prefill_fast_configure(tla_layer* L);
+cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
+                                void* out, cudaStream_t stream);
+
+}  // namespace tla
