@@ -353,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       const int s = it % C::kStages;
       const uint32_t ph = (it / C::kStages) & 1u;
       if (!flags[0] && !mbar_wait(&full[s], ph, a.error)) flags[0] = 1;
+      __syncwarp();
       uint8_t* kst = stages + s * C::kStageBytes;
       uint8_t* vst = kst + C::kTileBytes;
       const int y0 = lo + j * kTile;
@@ -536,11 +537,13 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
           const int r = i / (D + 2), e = i - r * (D + 2);
           float M = -INFINITY;
           for (int c = c0; c <= c1; ++c) {
+            if (cta_begin(c + 1, total, grid) == cta_begin(c, total, grid)) continue;  // empty range
             const int sl = cta_begin(c, total, grid) >= pb ? 0 : 1;
             M = fmaxf(M, __ldcg(p.scratch + ((static_cast<size_t>(c) * 2 + sl) * G + r) * (D + 2)));
           }
           float v = 0.f, Lsum = 0.f;
           for (int c = c0; c <= c1; ++c) {
+            if (cta_begin(c + 1, total, grid) == cta_begin(c, total, grid)) continue;
             const int sl = cta_begin(c, total, grid) >= pb ? 0 : 1;
             const float* pc = p.scratch + ((static_cast<size_t>(c) * 2 + sl) * G + r) * (D + 2);
             const float w = ex2(__ldcg(pc) - M);

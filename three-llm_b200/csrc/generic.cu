@@ -46,10 +46,12 @@ __device__ __forceinline__ float block_reduce_sum(float v, float* red) {
 }
 
 // One block per (t, b) token row of qkv.
-template <typename IO, typename CT>
+// QH: rotated queries as fp16 head-major [B][Hq][S][D] (the tensor-core
+// prefill's TMA source) instead of float32 [B][S][Hq][D].
+template <typename IO, typename CT, bool QH>
 __global__ void __launch_bounds__(kThreads) rope_append_kernel(LayerArgs a, const IO* __restrict__ qkv,
                                                                const int32_t* __restrict__ start, int seq_len,
-                                                               int slot_offset, int append, float* __restrict__ qscr) {
+                                                               int slot_offset, int append, void* __restrict__ qscr) {
   extern __shared__ float smem[];
   const int t = blockIdx.x, b = blockIdx.y;
   const int D = a.D, Hq = a.Hq, Hk = a.Hk;
@@ -118,7 +120,10 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(LayerArgs a, cons
       }
     }
     if (h < Hq) {
-      qscr[((static_cast<size_t>(b) * seq_len + t) * Hq + h) * D + d] = val;
+      if (QH)
+        static_cast<__half*>(qscr)[((static_cast<size_t>(b) * Hq + h) * seq_len + t) * D + d] = __float2half_rn(val);
+      else
+        static_cast<float*>(qscr)[((static_cast<size_t>(b) * seq_len + t) * Hq + h) * D + d] = val;
     } else {
       const int kh = h - Hq;
       CT* kc = static_cast<CT*>(a.k_cache);
@@ -205,12 +210,12 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-template <typename IO, typename CT>
+template <typename IO, typename CT, bool QH = false>
 cudaError_t rope_append_t(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
-                          int slot_offset, int append, float* qscr, cudaStream_t stream) {
+                          int slot_offset, int append, void* qscr, cudaStream_t stream) {
   const LayerArgs a = layer_args(L);
   const size_t smem = sizeof(float) * (static_cast<size_t>(L->Hq + 2 * L->Hk) * L->D + 2 * (L->rotary / 2 + 1) + 4);
-  auto k = rope_append_kernel<IO, CT>;
+  auto k = rope_append_kernel<IO, CT, QH>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
@@ -233,6 +238,12 @@ cudaError_t attend_t(const tla_layer* L, const float* qscr, const int32_t* start
 }
 
 }  // namespace
+
+cudaError_t launch_rope_append_half_q(const tla_layer* L, const void* qkv, const int32_t* start, int batch,
+                                      int seq_len, __half* qscr, cudaStream_t stream) {
+  if (L->io_fp32) return rope_append_t<float, __half, true>(L, qkv, start, batch, seq_len, 0, 1, qscr, stream);
+  return rope_append_t<__half, __half, true>(L, qkv, start, batch, seq_len, 0, 1, qscr, stream);
+}
 
 cudaError_t launch_rope_append(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
                                int slot_offset, int append, float* qscr, cudaStream_t stream) {

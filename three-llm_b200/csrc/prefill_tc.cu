@@ -1,13 +1,437 @@
-// Tensor-core causal prefill (tcgen05 / TMEM / TMA). Placeholder until the
-// kernel lands: every layer takes the generic path.
+// Causal prefill attention on the 5th-generation tensor cores (tcgen05),
+// fp16 K/V cache, head_dim 64 or 128.
+//
+// The reference has no prefill kernel: it replays the one-token decode graph
+// for every prompt position (packages/three-llm/src/decoder/DecoderTSLRunner.ts:
+// 472-480, 504-530), so position p attends to cache slots [window start, p]
+// with every earlier prompt token already appended. This kernel computes the
+// same outputs for a whole prompt chunk at once.
+//
+// One CTA per (128-row query tile, head, sequence), longest tiles first.
+// Warp roles (192 threads):
+//   warps 0-3  softmax: thread r owns query row r = TMEM lane r
+//   warp 4     TMA producer (Q tile once, then K/V tiles through a 2-stage ring)
+//   warp 5     MMA issuer: S = Q K^T (M=128, N=128, K=head_dim) into one of two
+//              TMEM S buffers, O_tile = P V (M=128, N=head_dim, K=128) into one
+//              of two TMEM O buffers; tcgen05.commit signals mbarriers.
+// P goes through shared memory in the canonical 128-byte-swizzled K-major
+// layout. The softmax warps keep the running max / sum and the output rows in
+// fp32 registers and fold each O_tile in one tile late, so the tensor core
+// computes S(n+1) and PV(n) while the softmax works on tile n.
+// Every mbarrier wait is bounded; on timeout the CTA records TLA_ERR_TIMEOUT,
+// stops waiting, runs its remaining control flow and frees its TMEM.
+#include <math.h>
+
+#include "tla_device.cuh"
 #include "tla_internal.h"
 
 namespace tla {
+
+namespace {
+
+constexpr int kRows = 128;       // query rows per CTA (TMEM lanes)
+constexpr int kCols = 128;       // kv tokens per tile
+constexpr int kThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D>
+struct PCfg {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kBoxBytes = 128 * 128;          // [128 rows][64 fp16]
+  static constexpr int kTileBytes = kBoxes * kBoxBytes;
+  static constexpr int kPB = D == 64 ? 2 : 1;           // P buffers
+  static constexpr int kPBytes = 2 * kBoxBytes;        // [128 rows][128 fp16]
+  static constexpr int kQ = 0;
+  static constexpr int kK = kQ + kTileBytes;           // 2 stages
+  static constexpr int kV = kK + 2 * kTileBytes;       // 2 stages
+  static constexpr int kP = kV + 2 * kTileBytes;
+  static constexpr int kBar = kP + kPB * kPBytes;
+  static constexpr int kNumBars = 1 + 2 + 2 + 2 + 2 + 2 + 2 * kPB + 2 + 2;
+  static constexpr int kSmem = kBar + kNumBars * 8 + 16 + 1024;
+  static constexpr uint32_t kTmemCols = 512;           // S 2x128 + O 2xD
+  static constexpr int kTmemO = 256;
+};
+
+struct PrefillParams {
+  CUtensorMap tm_q;  // rotated queries [B*Hq][S][D] fp16
+  CUtensorMap tm_k;  // cache [max_batch*Hk][max_tokens][D] fp16, 128-token boxes
+  CUtensorMap tm_v;
+  void* out;
+  const int32_t* start;
+  int* error;
+  int S, Hq, Hk, G, sliding, batch, num_m;
+  float scale_log2;
+};
+
+// ---------------------------------------------------------------- tcgen05 helpers
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  // sm_100 shared-memory matrix descriptor, 128-byte swizzle, version 1
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: fp16 A and B, fp32 accumulator, A K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool b_mn_major) {
+  return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int D, typename OUT>
+__global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
+  using C = PCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = bars + 3;
+  uint64_t* kv_empty = bars + 5;
+  uint64_t* s_full = bars + 7;
+  uint64_t* s_free = bars + 9;
+  uint64_t* p_full = bars + 11;
+  uint64_t* p_free = p_full + C::kPB;
+  uint64_t* o_full = p_free + C::kPB;
+  uint64_t* o_free = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // ---- work unit
+  const int bh_count = p.batch * p.Hq;
+  const int m = p.num_m - 1 - static_cast<int>(blockIdx.x) / bh_count;
+  const int bh = static_cast<int>(blockIdx.x) % bh_count;
+  const int b = bh / p.Hq, h = bh - b * p.Hq, kvh = h / p.G;
+  const int start = p.start[b];
+  const int row0 = m * kRows;
+  const int rows = min(kRows, p.S - row0);
+  const int pmin = start + row0, pmax = start + row0 + rows - 1;
+  const int first_min = p.sliding > 0 ? max(0, pmin - p.sliding + 1) : 0;
+  const int j0 = first_min / kCols, j1 = pmax / kCols;
+  const int ntiles = j1 - j0 + 1;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], kRows);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], kRows);
+    }
+    for (int i = 0; i < C::kPB; ++i) {
+      mbar_init(&p_full[i], kRows);
+      mbar_init(&p_free[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    if (*abort_flag) return;
+    if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
+  };
+
+  if (warp == 4) {
+    // ================================================================ TMA producer
+    if (lane == 0) {
+      tma_prefetch(&p.tm_q);
+      tma_prefetch(&p.tm_k);
+      tma_prefetch(&p.tm_v);
+      mbar_arrive_expect_tx(q_full, C::kTileBytes);
+#pragma unroll
+      for (int x = 0; x < C::kBoxes; ++x)
+        tma_load_3d(smem + C::kQ + x * C::kBoxBytes, &p.tm_q, q_full, x * 64, row0, b * p.Hq + h);
+      for (int n = 0; n < ntiles; ++n) {
+        const int st = n & 1;
+        wait(&kv_empty[st], ((n >> 1) & 1) ^ 1);
+        if (*abort_flag) continue;
+        const int y = (j0 + n) * kCols, z = b * p.Hk + kvh;
+        mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
+#pragma unroll
+        for (int x = 0; x < C::kBoxes; ++x)
+          tma_load_3d(smem + C::kK + st * C::kTileBytes + x * C::kBoxBytes, &p.tm_k, &k_full[st], x * 64, y, z);
+        mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
+#pragma unroll
+        for (int x = 0; x < C::kBoxes; ++x)
+          tma_load_3d(smem + C::kV + st * C::kTileBytes + x * C::kBoxBytes, &p.tm_v, &v_full[st], x * 64, y, z);
+      }
+      // no copies may be in flight when the CTA exits
+      for (int n = max(0, ntiles - 2); n < ntiles; ++n) {
+        wait(&k_full[n & 1], (n >> 1) & 1);
+        wait(&v_full[n & 1], (n >> 1) & 1);
+      }
+    }
+  } else if (warp == 5) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdS = idesc_f16(kRows, kCols, false);
+      constexpr uint32_t kIdO = idesc_f16(kRows, D, true);
+      const uint32_t q_base = smem_u32(smem + C::kQ);
+      wait(q_full, 0);
+      for (int n = 0; n <= ntiles; ++n) {
+        if (n < ntiles) {
+          const int st = n & 1, sb = n & 1;
+          wait(&k_full[st], (n >> 1) & 1);
+          wait(&s_free[sb], ((n >> 1) & 1) ^ 1);
+          tc_fence_after();
+          const uint32_t k_base = smem_u32(smem + C::kK + st * C::kTileBytes);
+          if (!*abort_flag) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * C::kBoxBytes + (kk & 3) * 32;
+              mma_f16(tmem + sb * kCols, sdesc(q_base + off, 16, 1024), sdesc(k_base + off, 16, 1024), kIdS,
+                      kk > 0 ? 1u : 0u);
+            }
+          }
+          mma_commit(&s_full[sb]);
+        }
+        if (n >= 1) {
+          const int q = n - 1, st = q & 1, ob = q & 1, pb = q % C::kPB;
+          wait(&p_full[pb], (q / C::kPB) & 1);
+          wait(&v_full[st], (q >> 1) & 1);
+          wait(&o_free[ob], ((q >> 1) & 1) ^ 1);
+          tc_fence_after();
+          const uint32_t p_base = smem_u32(smem + C::kP + pb * C::kPBytes);
+          const uint32_t v_base = smem_u32(smem + C::kV + st * C::kTileBytes);
+          if (!*abort_flag) {
+#pragma unroll
+            for (int kk = 0; kk < kCols / 16; ++kk)
+              mma_f16(tmem + C::kTmemO + ob * D, sdesc(p_base + (kk >> 2) * C::kBoxBytes + (kk & 3) * 32, 16, 1024),
+                      sdesc(v_base + kk * 2048, C::kBoxBytes, 1024), kIdO, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&o_full[ob]);
+          mma_commit(&kv_empty[st]);
+          mma_commit(&p_free[pb]);
+        }
+      }
+    }
+  } else {
+    // ================================================================ softmax (row r = tid)
+    const int r = tid;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int pr = start + row0 + r;
+    const int first_r = p.sliding > 0 ? max(0, pr - p.sliding + 1) : 0;
+    const float sl2 = p.scale_log2;
+    float o[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
+    auto absorb = [&](int q) {
+      const int ob = q & 1;
+      wait(&o_full[ob], (q >> 1) & 1);
+      __syncwarp();
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tmem_ld32(lane_addr + C::kTmemO + ob * D + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + v[i];
+      }
+      tc_fence_before();
+      mbar_arrive(&o_free[ob]);
+    };
+    for (int n = 0; n < ntiles; ++n) {
+      const int sb = n & 1, pb = n % C::kPB;
+      const int tok0 = (j0 + n) * kCols;
+      const bool masked = tok0 + kCols - 1 > pr || tok0 < first_r;
+      wait(&s_full[sb], (n >> 1) & 1);
+      __syncwarp();
+      tc_fence_after();
+      const uint32_t s_addr = lane_addr + sb * kCols;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kCols / 32; ++c) {
+        float v[32];
+        tmem_ld32(s_addr + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int tok = tok0 + c * 32 + i;
+          const bool ok = !masked || (tok >= first_r && tok <= pr);
+          mx = fmaxf(mx, ok ? v[i] : -INFINITY);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx * sl2);
+      const float mu = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = ex2(m_run - mu);
+      wait(&p_free[pb], ((n / C::kPB) & 1) ^ 1);
+      __syncwarp();
+      uint8_t* prow = smem + C::kP + pb * C::kPBytes + r * 128;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kCols / 32; ++c) {
+        float v[32];
+        tmem_ld32(s_addr + c * 32, v);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int tok = tok0 + c * 32 + i;
+          const bool ok0 = !masked || (tok >= first_r && tok <= pr);
+          const bool ok1 = !masked || (tok + 1 >= first_r && tok + 1 <= pr);
+          const float e0 = ok0 ? ex2(v[i] * sl2 - mu) : 0.f;
+          const float e1 = ok1 ? ex2(v[i + 1] * sl2 - mu) : 0.f;
+          sum += e0 + e1;
+          pk[i / 2] = pack_half2(e0, e1);
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int cc = c * 4 + q4;  // 16-byte chunk 0..15 of the 256-byte row
+          const int box = cc >> 3, ch = cc & 7;
+          *reinterpret_cast<uint4*>(prow + box * C::kBoxBytes + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(pk[q4 * 4], pk[q4 * 4 + 1], pk[q4 * 4 + 2], pk[q4 * 4 + 3]);
+        }
+      }
+      l_run = l_run * alpha + sum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[pb]);
+      mbar_arrive(&s_free[sb]);
+      if (n >= 1) absorb(n - 1);
+      alpha_prev = alpha;
+      m_run = m_new;
+    }
+    absorb(ntiles - 1);
+    // ---- epilogue: normalise and store this row
+    if (r < rows) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      OUT* dst = static_cast<OUT*>(p.out) + ((static_cast<size_t>(b) * p.S + row0 + r) * p.Hq + h) * D;
+      if constexpr (sizeof(OUT) == 2) {
+#pragma unroll
+        for (int i = 0; i < D; i += 8) {
+          uint4 u = make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv), pack_half2(o[i + 2] * inv, o[i + 3] * inv),
+                               pack_half2(o[i + 4] * inv, o[i + 5] * inv), pack_half2(o[i + 6] * inv, o[i + 7] * inv));
+          *reinterpret_cast<uint4*>(dst + i) = u;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < D; i += 4)
+          *reinterpret_cast<float4*>(dst + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
+  }
+}
+
+CUresult make_map(const tla_layer* L, void* base, uint64_t rows, uint64_t planes, CUtensorMap* map) {
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(L->D), rows, planes};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(L->D) * 2, static_cast<cuuint64_t>(L->D) * 2 * rows};
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return L->ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <int D, typename OUT>
+cudaError_t set_smem() {
+  return cudaFuncSetAttribute(prefill_tc_kernel<D, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              PCfg<D>::kSmem);
+}
+
+}  // namespace
+
 cudaError_t prefill_fast_configure(tla_layer* L) {
   L->fast_prefill = false;
+  if (L->cache_fp32 || (L->D != 64 && L->D != 128) || L->G <= 0 || L->ctx->encode_tiled == nullptr) return cudaSuccess;
+  const uint64_t planes = static_cast<uint64_t>(L->max_batch) * L->Hk;
+  if (make_map(L, L->k_cache, L->max_tokens, planes, &L->tmap_k128) != CUDA_SUCCESS ||
+      make_map(L, L->v_cache, L->max_tokens, planes, &L->tmap_v128) != CUDA_SUCCESS)
+    return cudaSuccess;
+  cudaError_t e;
+  if (L->D == 64) {
+    e = L->io_fp32 ? set_smem<64, float>() : set_smem<64, __half>();
+    L->prefill_smem = PCfg<64>::kSmem;
+  } else {
+    e = L->io_fp32 ? set_smem<128, float>() : set_smem<128, __half>();
+    L->prefill_smem = PCfg<128>::kSmem;
+  }
+  if (e != cudaSuccess) return e;
+  L->fast_prefill = true;
   return cudaSuccess;
 }
-cudaError_t launch_prefill_fast(const tla_layer*, const void*, const int32_t*, int, int, void*, cudaStream_t) {
-  return cudaErrorNotSupported;
+
+cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
+                                void* out, cudaStream_t stream) {
+  __half* qh = static_cast<__half*>(L->ctx->d_qscratch);
+  cudaError_t e = launch_rope_append_half_q(L, qkv, start, batch, seq_len, qh, stream);
+  if (e != cudaSuccess) return e;
+  PrefillParams p;
+  if (make_map(L, qh, seq_len, static_cast<uint64_t>(batch) * L->Hq, &p.tm_q) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  p.tm_k = L->tmap_k128;
+  p.tm_v = L->tmap_v128;
+  p.out = out;
+  p.start = start;
+  p.error = L->ctx->d_error;
+  p.S = seq_len;
+  p.Hq = L->Hq;
+  p.Hk = L->Hk;
+  p.G = L->G;
+  p.sliding = L->sliding;
+  p.batch = batch;
+  p.num_m = (seq_len + kRows - 1) / kRows;
+  p.scale_log2 = L->attn_scale * kLog2e;
+  const dim3 grid(static_cast<unsigned>(p.num_m * batch * L->Hq));
+  if (L->D == 64) {
+    if (L->io_fp32)
+      prefill_tc_kernel<64, float><<<grid, kThreads, PCfg<64>::kSmem, stream>>>(p);
+    else
+      prefill_tc_kernel<64, __half><<<grid, kThreads, PCfg<64>::kSmem, stream>>>(p);
+  } else {
+    if (L->io_fp32)
+      prefill_tc_kernel<128, float><<<grid, kThreads, PCfg<128>::kSmem, stream>>>(p);
+    else
+      prefill_tc_kernel<128, __half><<<grid, kThreads, PCfg<128>::kSmem, stream>>>(p);
+  }
+  return cudaGetLastError();
 }
+
 }  // namespace tla

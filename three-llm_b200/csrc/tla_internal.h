@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include "tla_api.h"
@@ -44,8 +45,10 @@ struct tla_layer {
   int decode_grid = 0;          // persistent CTAs per launch
   size_t decode_smem = 0;
   CUtensorMap tmap_k{}, tmap_v{};
-  // tensor-core prefill path
+  // tensor-core prefill path (cache maps with 128-token boxes)
   bool fast_prefill = false;
+  size_t prefill_smem = 0;
+  CUtensorMap tmap_k128{}, tmap_v128{};
 };
 
 namespace tla {
@@ -78,6 +81,9 @@ cudaError_t launch_rope_append(const tla_layer* L, const void* qkv, const int32_
 cudaError_t launch_attend_generic(const tla_layer* L, const float* qscr, const int32_t* start, int batch,
                                   int seq_len, int slot_offset, int local_tokens, const void* gate, void* out,
                                   float* partial, cudaStream_t stream);
+// rope_append with the rotated queries written as fp16 [B][Hq][S][D] (fp16 cache only).
+cudaError_t launch_rope_append_half_q(const tla_layer* L, const void* qkv, const int32_t* start, int batch,
+                                      int seq_len, __half* qscr, cudaStream_t stream);
 // Fast persistent split-KV decode (TMA + tensor-core tiles); partial != null
 // switches to partial-triple output (sequence sharding).
 cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_t* positions, const void* gate,
