@@ -296,3 +296,49 @@ def test_sequence_shards_combine_equals_full_decode(pkg, cuda, D):
     out = pkg.combine_lse(torch.stack(parts)).float().cpu().numpy()
     exp = oracle.decode_batch(qkv, [T], kc, vc, threads=8, **oracle_opts(Hq, Hk, D, rope_theta=500000.0))
     assert_close(out, exp, what="LSE combine of sequence shards")
+
+
+def test_config2_full_size_vs_torch_fp32(pkg, cuda):
+    """BASELINE config 2 at full size for one layer (batch 64, 4096 cached + 1 new, 32/8 heads,
+    d64, theta 5e5) against a float32 PyTorch restatement over the same cache contents."""
+    import math
+
+    from three_llm_b200.attention import rope_parameters
+    from tests.test_prefill_gpu import torch_rope
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    B, T, Hq, Hk, D = 64, 4096, 32, 8, 64
+    g = torch.Generator(device=cuda)
+    g.manual_seed(4)
+    layer = pkg.CUDAAttention(None, Hq * D, Hq, T + 1, {"headDim": D, "kvHeadCount": Hk, "ropeTheta": 5e5,
+                                                        "maxBatch": B, "dtype": torch.float16})
+    view = layer.cache_view()
+    n = B * Hk * (T + 1) * D
+
+    class Arr:
+        def __init__(self, ptr):
+            self.__cuda_array_interface__ = {"shape": (B, Hk, T + 1, D), "typestr": "<f2", "data": (ptr, False),
+                                             "version": 3}
+
+    kc = torch.as_tensor(Arr(view.key), device=cuda)
+    vc = torch.as_tensor(Arr(view.value), device=cuda)
+    kc.normal_(generator=g)
+    vc.normal_(generator=g)
+    qkv = torch.randn(B, (Hq + 2 * Hk) * D, generator=g, device=cuda).half()
+    pos = torch.full((B,), T, dtype=torch.int32, device=cuda)
+    out = layer.decode(qkv, pos).float()
+    assert layer.context.error() == 0
+    inv, _ = rope_parameters(D, 5e5)
+    inv = torch.from_numpy(inv).to(cuda)
+    x = qkv.float().view(B, Hq + 2 * Hk, 1, D)
+    p1 = torch.tensor([T], device=cuda)
+    q = torch_rope(x[:, :Hq], p1, inv, D)                      # [B, Hq, 1, D]
+    knew = torch_rope(x[:, Hq:Hq + Hk], p1, inv, D).half()     # stored fp16 in the cache
+    assert bool(torch.all((kc[:, :, T:T + 1].float() - knew.float()).abs() <= 2e-3)), "appended key"
+    k = kc.float().repeat_interleave(Hq // Hk, dim=1)          # [B, Hq, T+1, D] (slot T = new key)
+    v = vc.float().repeat_interleave(Hq // Hk, dim=1)
+    s = (q @ k.transpose(-1, -2)) / math.sqrt(D)
+    ref = (torch.softmax(s, dim=-1) @ v).reshape(B, Hq * D)
+    err = (out - ref).abs()
+    assert bool(torch.all(err <= 2e-3 + 1e-2 * ref.abs())), f"max abs err {err.max().item():.3e}"
+    del n

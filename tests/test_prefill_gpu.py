@@ -2,6 +2,8 @@
 which replays the one-token step at positions start..start+S-1
 (packages/three-llm/src/decoder/DecoderTSLRunner.ts:504-530). Outputs for
 every position and the cache contents must agree with the oracle."""
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -77,3 +79,49 @@ def test_prefill_then_decode_continues(pkg, cuda):
                        torch.tensor([S], dtype=torch.int32, device=cuda)).float().cpu().numpy()
     assert layer.context.error() == 0
     assert_close(out, exp[:, S], what="decode after prefill")
+
+
+@pytest.mark.parametrize("rotary", [18, 32])
+def test_prefill_partial_rotary_yarn_vnorm(pkg, cuda, rotary):
+    # rotary 18 takes the block-per-token RoPE kernel, rotary 32 the warp-per-token one
+    yarn = {"type": "yarn", "factor": 4.0, "original_context_length": 128.0, "beta_fast": 32.0, "beta_slow": 1.0}
+    prefill_case(pkg, cuda, 8, 2, 64, 160, [0, 20], 256,
+                 layer_kw={"ropeTheta": 10000.0, "rotaryDim": rotary, "ropeScaling": yarn, "vNorm": True},
+                 oracle_kw={"rope_theta": 10000.0, "rotary_dim": rotary, "rope_scaling": yarn, "v_norm": True})
+
+
+def torch_rope(x, pos, inv_freq, rotary, attn_factor=1.0):
+    """float32 rotate-half RoPE with float64 angles (x [..., T, D], pos [T])."""
+    ang = pos.double()[:, None] * inv_freq.double()[None, :]
+    c, s = torch.cos(ang).float(), torch.sin(ang).float()
+    half = rotary // 2
+    x1, x2, rest = x[..., :half], x[..., half:rotary], x[..., rotary:]
+    return torch.cat([(x1 * c - x2 * s) * attn_factor, (x2 * c + x1 * s) * attn_factor, rest], dim=-1)
+
+
+def test_prefill_config3_full_size_vs_torch_fp32(pkg, cuda):
+    """BASELINE config 3 at full size (4 x 2048 tokens, 14/2 heads, d64, theta 1e6)
+    against a float32 PyTorch restatement of the same causal attention."""
+    from three_llm_b200.attention import rope_parameters
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    B, S, Hq, Hk, D, T = 4, 2048, 14, 2, 64, 4096
+    g = torch.Generator(device=cuda)
+    g.manual_seed(3)
+    qkv = torch.randn(B, S, (Hq + 2 * Hk) * D, generator=g, device=cuda).half()
+    layer = pkg.CUDAAttention(None, Hq * D, Hq, T, {"headDim": D, "kvHeadCount": Hk, "ropeTheta": 1e6, "maxBatch": B,
+                                                    "dtype": torch.float16})
+    out = layer.prefill(qkv, torch.zeros(B, dtype=torch.int32, device=cuda)).float()
+    assert layer.context.error() == 0
+    inv, _ = rope_parameters(D, 1e6)
+    inv = torch.from_numpy(inv).to(cuda)
+    x = qkv.float().view(B, S, Hq + 2 * Hk, D).transpose(1, 2)  # [B, H, S, D]
+    pos = torch.arange(S, device=cuda)
+    q = torch_rope(x[:, :Hq], pos, inv, D)
+    k = torch_rope(x[:, Hq:Hq + Hk], pos, inv, D).repeat_interleave(Hq // Hk, dim=1)
+    v = x[:, Hq + Hk:].repeat_interleave(Hq // Hk, dim=1)
+    s = (q @ k.transpose(-1, -2)) / math.sqrt(D)
+    s = s.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool, device=cuda), 1), float("-inf"))
+    ref = (torch.softmax(s, dim=-1) @ v).transpose(1, 2).reshape(B, S, Hq * D)
+    err = (out - ref).abs()
+    assert bool(torch.all(err <= 2e-3 + 1e-2 * ref.abs())), f"max abs err {err.max().item():.3e}"

@@ -239,8 +239,109 @@ cudaError_t attend_t(const tla_layer* L, const float* qscr, const int32_t* start
 
 }  // namespace
 
+// Warp-per-token variant for head_dim 64 / 128 and an fp16 cache: lane l holds
+// elements [l*EPL, (l+1)*EPL) of every head of the token, head norms are warp
+// reductions and the rotate-half partner comes from lane +/- half/EPL.
+template <typename IO, int D>
+__global__ void __launch_bounds__(128) rope_append_warp_kernel(LayerArgs a, const IO* __restrict__ qkv,
+                                                               const int32_t* __restrict__ start, int seq_len,
+                                                               int tokens, __half* __restrict__ qscr) {
+  constexpr int EPL = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int ti = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (ti >= tokens) return;
+  const int b = ti / seq_len, t = ti - b * seq_len;
+  const int Hq = a.Hq, Hk = a.Hk;
+  const int pos = start[b] + t;
+  if (pos < 0 || pos >= a.max_tokens) {
+    if (lane == 0) report_error(a.error, TLA_ERR_POSITION);
+    return;
+  }
+  const int half = a.rotary / 2;
+  const int d0 = lane * EPL;
+  const bool lo_side = d0 < half;
+  const bool rot = half > 0 && d0 < a.rotary;
+  const int src = !rot ? lane : (lo_side ? lane + half / EPL : lane - half / EPL);
+  float c[EPL], sn[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    c[e] = 1.f;
+    sn[e] = 0.f;
+    const int j = lo_side ? d0 + e : d0 + e - half;
+    if (rot && j < a.pair_count) rope_cos_sin(pos, a.inv_freq[j], &c[e], &sn[e]);
+  }
+  const int heads = Hq + 2 * Hk;
+  const IO* row = qkv + static_cast<size_t>(ti) * heads * D;
+  __half* kc = static_cast<__half*>(a.k_cache);
+  __half* vc = static_cast<__half*>(a.v_cache);
+  for (int hh = 0; hh < heads; ++hh) {
+    float x[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) x[e] = to_f32(row[hh * D + d0 + e]);
+    const float* w = hh < Hq ? a.q_norm : (hh < Hq + Hk ? a.k_norm : nullptr);
+    const bool norm = hh < Hq + Hk ? w != nullptr : a.v_norm != 0;
+    if (norm) {  // math.ts:78-97
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) ss += x[e] * x[e];
+      ss = warp_sum(ss);
+      const float inv_rms = 1.f / sqrtf(ss / static_cast<float>(D) + a.rms_eps);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const float sc = w == nullptr ? 1.f : (a.offset_rms ? 1.f + w[d0 + e] : w[d0 + e]);
+        x[e] = x[e] * inv_rms * sc;
+      }
+    }
+    if (hh < Hq + Hk) {  // RoPE, math.ts:134-147
+      float y[EPL];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const float partner = __shfl_sync(0xffffffffu, x[e], src);
+        y[e] = x[e];
+        const int j = lo_side ? d0 + e : d0 + e - half;
+        if (rot && j < a.pair_count) y[e] = (x[e] * c[e] + (lo_side ? -partner : partner) * sn[e]) * a.attn_factor;
+      }
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) x[e] = y[e];
+    }
+    __half hv[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) hv[e] = __float2half_rn(x[e]);
+    __half* dst;
+    if (hh < Hq)
+      dst = qscr + ((static_cast<size_t>(b) * Hq + hh) * seq_len + t) * D + d0;
+    else if (hh < Hq + Hk)
+      dst = kc + ((static_cast<size_t>(b) * Hk + (hh - Hq)) * a.max_tokens + pos) * D + d0;
+    else
+      dst = vc + ((static_cast<size_t>(b) * Hk + (hh - Hq - Hk)) * a.max_tokens + pos) * D + d0;
+    if constexpr (EPL == 2)
+      *reinterpret_cast<__half2*>(dst) = __halves2half2(hv[0], hv[1]);
+    else
+      *reinterpret_cast<uint2*>(dst) = make_uint2(*reinterpret_cast<uint32_t*>(&hv[0]),
+                                                  *reinterpret_cast<uint32_t*>(&hv[2]));
+  }
+}
+
+template <typename IO, int D>
+cudaError_t rope_warp_t(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
+                        __half* qscr, cudaStream_t stream) {
+  const int tokens = batch * seq_len;
+  rope_append_warp_kernel<IO, D><<<(tokens + 3) / 4, 128, 0, stream>>>(layer_args(L), static_cast<const IO*>(qkv),
+                                                                         start, seq_len, tokens, qscr);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_rope_append_half_q(const tla_layer* L, const void* qkv, const int32_t* start, int batch,
                                       int seq_len, __half* qscr, cudaStream_t stream) {
+  const int epl = L->D / 32;
+  const bool warp_ok = !L->cache_fp32 && (L->D == 64 || L->D == 128) && ((L->rotary / 2) % epl == 0);
+  if (warp_ok) {
+    if (L->D == 64)
+      return L->io_fp32 ? rope_warp_t<float, 64>(L, qkv, start, batch, seq_len, qscr, stream)
+                        : rope_warp_t<__half, 64>(L, qkv, start, batch, seq_len, qscr, stream);
+    return L->io_fp32 ? rope_warp_t<float, 128>(L, qkv, start, batch, seq_len, qscr, stream)
+                      : rope_warp_t<__half, 128>(L, qkv, start, batch, seq_len, qscr, stream);
+  }
   if (L->io_fp32) return rope_append_t<float, __half, true>(L, qkv, start, batch, seq_len, 0, 1, qscr, stream);
   return rope_append_t<__half, __half, true>(L, qkv, start, batch, seq_len, 0, 1, qscr, stream);
 }

@@ -8,16 +8,20 @@
 // same outputs for a whole prompt chunk at once.
 //
 // One CTA per (128-row query tile, head, sequence), longest tiles first.
-// Warp roles (192 threads):
-//   warps 0-3  softmax: thread r owns query row r = TMEM lane r
-//   warp 4     TMA producer (Q tile once, then K/V tiles through a 2-stage ring)
-//   warp 5     MMA issuer: S = Q K^T (M=128, N=128, K=head_dim) into one of two
-//              TMEM S buffers, O_tile = P V (M=128, N=head_dim, K=128) into one
-//              of two TMEM O buffers; tcgen05.commit signals mbarriers.
+// Warp roles (kSoftmaxGroups * 128 + 64 threads):
+//   warps 0..4*NW-1  softmax: NW warpgroups; thread (g, r) owns query row r
+//                    (TMEM lane r) and columns [g*128/NW, (g+1)*128/NW) of
+//                    each S tile and [g*D/NW, (g+1)*D/NW) of the output row.
+//                    The NW partial row maxima meet in shared memory once per
+//                    tile; the row sums stay split until the epilogue.
+//   warp 4*NW        TMA producer (Q tile once, then K/V tiles through a 2-stage ring)
+//   warp 4*NW+1      MMA issuer: S = Q K^T (M=128, N=128, K=head_dim) into one of
+//                    two TMEM S buffers, O_tile = P V (M=128, N=head_dim, K=128)
+//                    into one of two TMEM O buffers; tcgen05.commit signals mbarriers.
 // P goes through shared memory in the canonical 128-byte-swizzled K-major
-// layout. The softmax warps keep the running max / sum and the output rows in
-// fp32 registers and fold each O_tile in one tile late, so the tensor core
-// computes S(n+1) and PV(n) while the softmax works on tile n.
+// layout. The softmax warps keep the running max / sum and their output
+// columns in fp32 registers and fold each O_tile in one tile late, so the
+// tensor core computes S(n+1) and PV(n) while the softmax works on tile n.
 // Every mbarrier wait is bounded; on timeout the CTA records TLA_ERR_TIMEOUT,
 // stops waiting, runs its remaining control flow and frees its TMEM.
 #include <math.h>
@@ -31,7 +35,9 @@ namespace {
 
 constexpr int kRows = 128;       // query rows per CTA (TMEM lanes)
 constexpr int kCols = 128;       // kv tokens per tile
-constexpr int kThreads = 192;
+constexpr int kNW = 4;                          // softmax warpgroups
+constexpr int kThreads = kNW * 128 + 64;
+constexpr int kSoftmaxThreads = kNW * 128;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
@@ -47,7 +53,8 @@ struct PCfg {
   static constexpr int kP = kV + 2 * kTileBytes;
   static constexpr int kBar = kP + kPB * kPBytes;
   static constexpr int kNumBars = 1 + 2 + 2 + 2 + 2 + 2 + 2 * kPB + 2 + 2;
-  static constexpr int kSmem = kBar + kNumBars * 8 + 16 + 1024;
+  static constexpr int kRed = kBar + kNumBars * 8 + 16;      // [2][kNW][128] row-max partials
+  static constexpr int kSmem = kRed + 2 * kNW * 128 * 4 + 1024;
   static constexpr uint32_t kTmemCols = 512;           // S 2x128 + O 2xD
   static constexpr int kTmemO = 256;
 };
@@ -108,6 +115,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]) {
+  static_assert(N % 16 == 0, "TMEM loads come in 16-column pieces");
+  if constexpr (N % 32 == 0) {
+#pragma unroll
+    for (int c = 0; c < N / 32; ++c) tmem_ld32(taddr + c * 32, *reinterpret_cast<float(*)[32]>(&v[c * 32]));
+  } else {
+#pragma unroll
+    for (int c = 0; c < N / 16; ++c) tmem_ld16(taddr + c * 16, *reinterpret_cast<float(*)[16]>(&v[c * 16]));
+  }
+}
+
 template <int D, typename OUT>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
   using C = PCfg<D>;
@@ -148,18 +180,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], kRows);
+      mbar_init(&s_free[i], kSoftmaxThreads);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], kRows);
+      mbar_init(&o_free[i], kSoftmaxThreads);
     }
     for (int i = 0; i < C::kPB; ++i) {
-      mbar_init(&p_full[i], kRows);
+      mbar_init(&p_full[i], kSoftmaxThreads);
       mbar_init(&p_free[i], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  constexpr int kProducerWarp = kNW * 4, kMmaWarp = kNW * 4 + 1;
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(C::kTmemCols)
                  : "memory");
@@ -174,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
   };
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ================================================================ TMA producer
     if (lane == 0) {
       tma_prefetch(&p.tm_q);
@@ -204,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         wait(&v_full[n & 1], (n >> 1) & 1);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ================================================================ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdS = idesc_f16(kRows, kCols, false);
@@ -249,82 +282,85 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       }
     }
   } else {
-    // ================================================================ softmax (row r = tid)
-    const int r = tid;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // ================================================================ softmax
+    constexpr int CW = kCols / kNW;  // S columns per thread
+    constexpr int DW = D / kNW;      // output columns per thread
+    const int g = warp >> 2;         // warpgroup
+    const int r = tid & 127;         // query row = TMEM lane
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const int pr = start + row0 + r;
     const int first_r = p.sliding > 0 ? max(0, pr - p.sliding + 1) : 0;
     const float sl2 = p.scale_log2;
-    float o[D];
+    float* red = reinterpret_cast<float*>(smem + C::kRed);  // [2][kNW][128]
+    float o[DW];
 #pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
+    for (int i = 0; i < DW; ++i) o[i] = 0.f;
+    float m_run = -INFINITY, l_part = 0.f, alpha_prev = 0.f;
     auto absorb = [&](int q) {
       const int ob = q & 1;
       wait(&o_full[ob], (q >> 1) & 1);
       __syncwarp();
       tc_fence_after();
+      float v[DW];
+      tmem_ld<DW>(lane_addr + C::kTmemO + ob * D + g * DW, v);
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        tmem_ld32(lane_addr + C::kTmemO + ob * D + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + v[i];
-      }
+      for (int i = 0; i < DW; ++i) o[i] = fmaf(o[i], alpha_prev, v[i]);
       tc_fence_before();
       mbar_arrive(&o_free[ob]);
     };
     for (int n = 0; n < ntiles; ++n) {
       const int sb = n & 1, pb = n % C::kPB;
-      const int tok0 = (j0 + n) * kCols;
-      const bool masked = tok0 + kCols - 1 > pr || tok0 < first_r;
+      const int tok0 = (j0 + n) * kCols + g * CW;  // first token of this thread's columns
+      const bool masked = tok0 + CW - 1 > pr || tok0 < first_r;
       wait(&s_full[sb], (n >> 1) & 1);
       __syncwarp();
       tc_fence_after();
-      const uint32_t s_addr = lane_addr + sb * kCols;
-      float mx = -INFINITY;
+      float sv[CW];
+      tmem_ld<CW>(lane_addr + sb * kCols + g * CW, sv);
+      if (masked) {
 #pragma unroll
-      for (int c = 0; c < kCols / 32; ++c) {
-        float v[32];
-        tmem_ld32(s_addr + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int tok = tok0 + c * 32 + i;
-          const bool ok = !masked || (tok >= first_r && tok <= pr);
-          mx = fmaxf(mx, ok ? v[i] : -INFINITY);
+        for (int i = 0; i < CW; ++i) {
+          const int tok = tok0 + i;
+          sv[i] = (tok >= first_r && tok <= pr) ? sv[i] : -INFINITY;
         }
       }
-      const float m_new = fmaxf(m_run, mx * sl2);
+      float mx[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+      for (int i = 4; i < CW; i += 4) {
+        mx[0] = fmaxf(mx[0], sv[i]);
+        mx[1] = fmaxf(mx[1], sv[i + 1]);
+        mx[2] = fmaxf(mx[2], sv[i + 2]);
+        mx[3] = fmaxf(mx[3], sv[i + 3]);
+      }
+      float* rb = red + (n & 1) * kNW * 128;
+      rb[g * 128 + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      named_barrier_sync(1, kSoftmaxThreads);
+      float mt = rb[r];
+#pragma unroll
+      for (int k = 1; k < kNW; ++k) mt = fmaxf(mt, rb[k * 128 + r]);
+      const float m_new = fmaxf(m_run, mt * sl2);
       const float mu = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = ex2(m_run - mu);
       wait(&p_free[pb], ((n / C::kPB) & 1) ^ 1);
       __syncwarp();
-      uint8_t* prow = smem + C::kP + pb * C::kPBytes + r * 128;
-      float sum = 0.f;
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[CW / 2];
 #pragma unroll
-      for (int c = 0; c < kCols / 32; ++c) {
-        float v[32];
-        tmem_ld32(s_addr + c * 32, v);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int tok = tok0 + c * 32 + i;
-          const bool ok0 = !masked || (tok >= first_r && tok <= pr);
-          const bool ok1 = !masked || (tok + 1 >= first_r && tok + 1 <= pr);
-          const float e0 = ok0 ? ex2(v[i] * sl2 - mu) : 0.f;
-          const float e1 = ok1 ? ex2(v[i + 1] * sl2 - mu) : 0.f;
-          sum += e0 + e1;
-          pk[i / 2] = pack_half2(e0, e1);
-        }
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int cc = c * 4 + q4;  // 16-byte chunk 0..15 of the 256-byte row
-          const int box = cc >> 3, ch = cc & 7;
-          *reinterpret_cast<uint4*>(prow + box * C::kBoxBytes + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(pk[q4 * 4], pk[q4 * 4 + 1], pk[q4 * 4 + 2], pk[q4 * 4 + 3]);
-        }
+      for (int i = 0; i < CW; i += 2) {
+        const float e0 = ex2(fmaf(sv[i], sl2, -mu));  // exp2(-inf) = 0 for masked tokens
+        const float e1 = ex2(fmaf(sv[i + 1], sl2, -mu));
+        sum[(i >> 1) & 3] += e0 + e1;
+        pk[i / 2] = pack_half2(e0, e1);
       }
-      l_run = l_run * alpha + sum;
+      uint8_t* prow = smem + C::kP + pb * C::kPBytes + r * 128;
+#pragma unroll
+      for (int q4 = 0; q4 < CW / 8; ++q4) {
+        const int cc = g * (CW / 8) + q4;  // 16-byte chunk 0..15 of the 256-byte P row
+        const int box = cc >> 3, ch = cc & 7;
+        *reinterpret_cast<uint4*>(prow + box * C::kBoxBytes + ((ch ^ (r & 7)) << 4)) =
+            make_uint4(pk[q4 * 4], pk[q4 * 4 + 1], pk[q4 * 4 + 2], pk[q4 * 4 + 3]);
+      }
+      l_part = fmaf(l_part, alpha, (sum[0] + sum[1]) + (sum[2] + sum[3]));
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[pb]);
@@ -334,27 +370,33 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       m_run = m_new;
     }
     absorb(ntiles - 1);
-    // ---- epilogue: normalise and store this row
+    // ---- epilogue: total row sum, normalise and store this thread's columns
+    float* rl = red + (ntiles & 1) * kNW * 128;  // the buffer the last tile did not use
+    rl[g * 128 + r] = l_part;
+    named_barrier_sync(1, kSoftmaxThreads);
+    float l_run = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNW; ++k) l_run += rl[k * 128 + r];
     if (r < rows) {
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      OUT* dst = static_cast<OUT*>(p.out) + ((static_cast<size_t>(b) * p.S + row0 + r) * p.Hq + h) * D;
+      OUT* dst = static_cast<OUT*>(p.out) + ((static_cast<size_t>(b) * p.S + row0 + r) * p.Hq + h) * D + g * DW;
       if constexpr (sizeof(OUT) == 2) {
 #pragma unroll
-        for (int i = 0; i < D; i += 8) {
+        for (int i = 0; i < DW; i += 8) {
           uint4 u = make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv), pack_half2(o[i + 2] * inv, o[i + 3] * inv),
                                pack_half2(o[i + 4] * inv, o[i + 5] * inv), pack_half2(o[i + 6] * inv, o[i + 7] * inv));
           *reinterpret_cast<uint4*>(dst + i) = u;
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < D; i += 4)
+        for (int i = 0; i < DW; i += 4)
           *reinterpret_cast<float4*>(dst + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
   }
