@@ -41,7 +41,8 @@ typedef enum tla_status {
   TLA_ERR_POSITION = -12,     /* device-reported: a position outside [0, max_tokens) */
   TLA_ERR_TIMEOUT = -13,      /* device-reported: a bounded in-kernel wait expired */
   TLA_ERR_NO_DEVICE = -14,
-  TLA_ERR_SHARED = -15        /* operation not allowed on a layer that borrows another's cache */
+  TLA_ERR_SHARED = -15,       /* operation not allowed on a layer that borrows another's cache */
+  TLA_ERR_SCRATCH_LIMIT = -16 /* request exceeds the fixed scratch of tla_decode_noalloc */
 } tla_status;
 
 /* RoPE scaling: RopeScalingConfig | YarnRoPEConfig (packages/three-llm/src/types.ts:245-256). */
@@ -177,6 +178,34 @@ int tla_cache_read(const tla_layer* layer, int32_t seq, int32_t token_begin, int
 /* Inverse of tla_cache_read: host float32 token-major rows into the cache. */
 int tla_cache_write(tla_layer* layer, int32_t seq, int32_t token_begin, int32_t count, const float* key,
                     const float* value);
+
+/* Allocation-free decode. No counterpart in the reference: this entry point
+ * serves hosts that cannot call cudaMalloc - hosts whose device memory is all
+ * owned by their own pool or a fixed budget, and serving loops that must not
+ * take cudaMalloc's implicit device-wide synchronisation - so it needs no
+ * tla_ctx or tla_layer and allocates nothing.
+ *
+ * It runs the same decode step as tla_decode on the calling thread's current
+ * device, with the caller's buffers: config as for tla_layer_create (fp16
+ * cache, head_dim 64 or 128, head_count a multiple of kv_head_count with a
+ * ratio of at most 16, max_batch <= 1024); key_cache / value_cache laid out
+ * [max_batch][kv_head_count][max_tokens][head_dim] (the new token is appended
+ * there); q_norm_weight / k_norm_weight device float32 [head_dim] or NULL;
+ * qkv, positions, gate, out as for tla_decode; status a device int32 that
+ * receives device-detected errors (TLA_ERR_POSITION, TLA_ERR_TIMEOUT) or NULL.
+ *
+ * Its scratch (split-KV partial results, completion counters, the RoPE table)
+ * is one static 8 MiB device array in the library, which every GPU that loads
+ * the library holds until the process exits. batch * kv_head_count may not
+ * exceed 16384 (TLA_ERR_SCRATCH_LIMIT otherwise). The first call on a device
+ * looks up that array's device address, so make that first call before any
+ * stream capture. Every call shares the array and keeps the last call's
+ * contents; calls whose execution overlaps on the GPU (for example on two
+ * streams) race on it and must be serialised by the caller. */
+int tla_decode_noalloc(const tla_attn_config* config, void* key_cache, void* value_cache,
+                       const float* q_norm_weight, const float* k_norm_weight, const void* qkv,
+                       const int32_t* positions, const void* gate, void* out, int32_t* status, int32_t batch,
+                       void* stream);
 
 #ifdef __cplusplus
 }

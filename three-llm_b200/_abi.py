@@ -16,6 +16,7 @@ STATUS = {
     -4: "TLA_ERR_ROPE_FACTOR", -5: "TLA_ERR_YARN_RANGE", -6: "TLA_ERR_YARN_FACTOR", -7: "TLA_ERR_LLAMA3_RANGE",
     -8: "TLA_ERR_ROTARY_DIM", -9: "TLA_ERR_UNSUPPORTED", -10: "TLA_ERR_CUDA", -11: "TLA_ERR_OUT_OF_MEMORY",
     -12: "TLA_ERR_POSITION", -13: "TLA_ERR_TIMEOUT", -14: "TLA_ERR_NO_DEVICE", -15: "TLA_ERR_SHARED",
+    -16: "TLA_ERR_SCRATCH_LIMIT",
 }
 ROPE_TYPES = {"default": 0, "none": 0, "linear": 1, "yarn": 2, "llama3": 3}
 FLAG_OFFSET_RMS_NORM = 1 << 0
@@ -27,6 +28,7 @@ EXPORTS = [
     "tla_status_string", "tla_create", "tla_destroy", "tla_get_error", "tla_rope_parameters", "tla_layer_create",
     "tla_layer_share_cache", "tla_layer_destroy", "tla_layer_cache_view", "tla_decode", "tla_prefill",
     "tla_decode_partial", "tla_combine_lse", "tla_cache_reset", "tla_cache_read", "tla_cache_write",
+    "tla_decode_noalloc",
 ]
 
 
@@ -111,6 +113,7 @@ def lib():
         L.tla_cache_reset.argtypes = [P, P]
         L.tla_cache_read.argtypes = [P, i32, i32, i32, P, P]
         L.tla_cache_write.argtypes = [P, i32, i32, i32, P, P]
+        L.tla_decode_noalloc.argtypes = [ctypes.POINTER(AttnConfig), P, P, P, P, P, P, P, P, P, i32, P]
         for name in EXPORTS:
             if name != "tla_status_string":
                 getattr(L, name).restype = ctypes.c_int

@@ -24,6 +24,8 @@
 // warp shuffles. All smem reads are ldmatrix on the swizzled layout.
 #include <math.h>
 
+#include <mutex>
+
 #include "tla_device.cuh"
 #include "tla_internal.h"
 
@@ -657,3 +659,135 @@ cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_
 }
 
 }  // namespace tla
+
+// ============================================================================
+// Allocation-free decode: the same persistent split-KV kernel, with its
+// scratch in a fixed static device array instead of memory owned by a tla_ctx.
+// ============================================================================
+namespace tla {
+namespace {
+
+// Per-device static scratch (every GPU that loads the library holds it until exit):
+//   [0, 64 KiB)            completion counters, int32[kStaticMaxPairs]
+//   [64 KiB, +256)         status word used when the caller passes none
+//   [+256, +512)           RoPE inverse frequencies, float[64]
+//   [+512, 8 MiB)          split-KV partial triples
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;
+constexpr int kStaticMaxPairs = 16384;  // batch * kv_head_count
+constexpr size_t kStaticStatusOff = size_t(kStaticMaxPairs) * 4;
+constexpr size_t kStaticInvFreqOff = kStaticStatusOff + 256;
+constexpr size_t kStaticPartialOff = kStaticInvFreqOff + 256;
+constexpr int kStaticMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+struct StaticScratchSlot {
+  std::once_flag once;
+  cudaError_t status = cudaSuccess;
+  unsigned char* ptr = nullptr;
+};
+StaticScratchSlot g_static_slots[kStaticMaxDevices];
+std::once_flag g_static_encode_once;
+PFN_cuTensorMapEncodeTiled_v12000 g_static_encode = nullptr;
+
+}  // namespace
+}  // namespace tla
+
+extern "C" int tla_decode_noalloc(const tla_attn_config* cfg, void* key_cache, void* value_cache,
+                                  const float* q_norm_weight, const float* k_norm_weight, const void* qkv,
+                                  const int32_t* positions, const void* gate, void* out, int32_t* status,
+                                  int32_t batch, void* stream) {
+  using namespace tla;
+  if (!cfg || !key_cache || !value_cache || !qkv || !positions || !out || batch < 0) return TLA_ERR_INVALID_ARG;
+  const int Hq = cfg->head_count, D = cfg->head_dim;
+  const int Hk = cfg->kv_head_count > 0 ? cfg->kv_head_count : Hq;
+  if (Hq <= 0 || D <= 0 || Hk > Hq || cfg->max_tokens <= 0 || cfg->max_batch <= 0 || batch > cfg->max_batch ||
+      cfg->sliding_window < 0)
+    return TLA_ERR_INVALID_ARG;
+  // Only the shapes of the fast kernel: fp16 cache, head_dim 64/128, GQA group <= 16.
+  if ((cfg->flags & TLA_FLAG_CACHE_FP32) || (D != 64 && D != 128) || Hq % Hk != 0 || Hq / Hk > 16 ||
+      cfg->max_batch > kMaxBatch)
+    return TLA_ERR_UNSUPPORTED;
+  if (static_cast<long long>(batch) * Hk > kStaticMaxPairs) return TLA_ERR_SCRATCH_LIMIT;
+  const int rotary = cfg->rotary_dim < 0 ? D : cfg->rotary_dim;
+  if (rotary % 2 != 0 || rotary > D) return TLA_ERR_ROTARY_DIM;
+  const bool rope_on = cfg->rope_theta > 0 && rotary > 0;
+  const int freq_dim = cfg->rope_freq_dim > 0 ? cfg->rope_freq_dim : rotary;
+  const int pair_count = cfg->rope_pair_count >= 0 ? cfg->rope_pair_count : rotary / 2;
+  float inv[64] = {0.f};
+  double af = 1;
+  if (rope_on) {
+    if (freq_dim / 2 > 64) return TLA_ERR_UNSUPPORTED;
+    const int rc = tla_rope_parameters(freq_dim, cfg->rope_theta, &cfg->rope_scaling, inv, &af);
+    if (rc != TLA_OK) return rc;
+    if (pair_count > freq_dim / 2) return TLA_ERR_INVALID_ARG;
+  }
+  if (batch == 0) return TLA_OK;
+
+  // One-time set-up per device, with that device current: the device address
+  // of the static array (its name is only a stand-in in host code).
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kStaticMaxDevices) return TLA_ERR_NO_DEVICE;
+  StaticScratchSlot& slot = g_static_slots[dev];
+  std::call_once(slot.once, [&slot] {
+    slot.status = cudaGetSymbolAddress(reinterpret_cast<void**>(&slot.ptr), g_static_scratch);
+  });
+  if (slot.status != cudaSuccess || slot.ptr == nullptr) return TLA_ERR_CUDA;
+  std::call_once(g_static_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_static_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_static_encode == nullptr) return TLA_ERR_CUDA;
+
+  // Host-side descriptions only: nothing below allocates device memory.
+  tla_ctx ctx;
+  ctx.device = dev;
+  if (cudaDeviceGetAttribute(&ctx.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return TLA_ERR_CUDA;
+  ctx.d_error = status ? status : reinterpret_cast<int*>(slot.ptr + kStaticStatusOff);
+  ctx.d_counters = reinterpret_cast<int32_t*>(slot.ptr);
+  ctx.counter_count = kStaticMaxPairs;
+  ctx.d_partials = reinterpret_cast<float*>(slot.ptr + kStaticPartialOff);
+  ctx.partial_floats = (kStaticScratchBytes - kStaticPartialOff) / sizeof(float);
+  ctx.encode_tiled = g_static_encode;
+  tla_layer L;
+  L.ctx = &ctx;
+  L.cfg = *cfg;
+  L.Hq = Hq;
+  L.Hk = Hk;
+  L.D = D;
+  L.G = Hq / Hk;
+  L.max_tokens = cfg->max_tokens;
+  L.max_batch = cfg->max_batch;
+  L.rotary = rope_on ? rotary : 0;
+  L.freq_half = rope_on ? freq_dim / 2 : 0;
+  L.pair_count = rope_on ? (pair_count < rotary / 2 ? pair_count : rotary / 2) : 0;
+  L.sliding = cfg->sliding_window;
+  L.attn_scale = static_cast<float>(cfg->has_attn_scale ? cfg->attn_scale : 1 / sqrt(static_cast<double>(D)));
+  L.attn_factor = static_cast<float>(af);
+  L.rms_eps = static_cast<float>(cfg->rms_epsilon > 0 ? cfg->rms_epsilon : 1e-6);
+  L.io_fp32 = (cfg->flags & TLA_FLAG_IO_FP32) != 0;
+  L.v_norm = (cfg->flags & TLA_FLAG_V_NORM) != 0;
+  L.offset_rms = (cfg->flags & TLA_FLAG_OFFSET_RMS_NORM) != 0;
+  L.k_cache = key_cache;
+  L.v_cache = value_cache;
+  L.d_inv_freq = reinterpret_cast<float*>(slot.ptr + kStaticInvFreqOff);
+  L.d_qnorm = const_cast<float*>(q_norm_weight);
+  L.d_knorm = const_cast<float*>(k_norm_weight);
+  if (decode_fast_configure(&L) != cudaSuccess || !L.fast_decode) return TLA_ERR_UNSUPPORTED;
+  const int per_cta = 2 * L.G * (D + 2);
+  const int max_grid = static_cast<int>(ctx.partial_floats / per_cta);
+  if (max_grid < 1) return TLA_ERR_SCRATCH_LIMIT;
+  if (L.decode_grid > max_grid) L.decode_grid = max_grid;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents: reload the RoPE table and
+  // zero the completion counters this launch uses.
+  if (cudaMemcpyAsync(L.d_inv_freq, inv, sizeof(inv), cudaMemcpyHostToDevice, st) != cudaSuccess) return TLA_ERR_CUDA;
+  if (cudaMemsetAsync(ctx.d_counters, 0, sizeof(int32_t) * batch * Hk, st) != cudaSuccess) return TLA_ERR_CUDA;
+  const cudaError_t e =
+      launch_decode_fast(&L, qkv, positions, gate, out, nullptr, batch, 0, cfg->max_tokens, 1, st);
+  return e == cudaSuccess ? TLA_OK : TLA_ERR_CUDA;
+}

@@ -148,6 +148,7 @@ const char* tla_status_string(int status) {
     case TLA_ERR_TIMEOUT: return "in-kernel wait timed out";
     case TLA_ERR_NO_DEVICE: return "no CUDA device";
     case TLA_ERR_SHARED: return "layer borrows another layer's cache";
+    case TLA_ERR_SCRATCH_LIMIT: return "request exceeds the fixed scratch of the allocation-free decode";
     default: return "unknown status";
   }
 }
