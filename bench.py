@@ -1,22 +1,30 @@
 """Benchmark of the B200 attention path (BASELINE.json metric).
 
-Default workload: 1B-class decode attention, 16 layers,
-32 query heads, 8 KV heads, head_dim 64, fp16 KV cache with 4096 cached
-tokens + 1 new token per sequence, batch 64, RoPE theta 5e5. One step = one
-decode token for every sequence through all 16 layers (append + attention).
-Inputs are synthetic (seeded N(0,1), fp16) and larger than L2 (8.6 GB of
-cache per step), so no L2 flush is needed between steps.
+Workloads (synthetic, seeded N(0,1) fp16 inputs; one step = one decode token
+for every sequence through every layer):
 
-Multi-GPU (torchrun): every rank runs the full workload on its own GPU
-(batch sharding: each rank owns 64 sequences), no collective on the data
-path; `value` is the aggregate over ranks divided by the slowest rank's time.
+  decode_1b  (default) 16 layers, 32 q / 8 kv heads, d64,
+             4096 cached + 1 new token, batch 64 per GPU, RoPE theta 5e5.
+             Multi-GPU: every rank owns its own 64 sequences (batch sharding,
+             weak scaling, no collective). The default line also carries
+             the config-3 prefill measurement under "prefill".
+  ragged_8b  (config 4) 32 layers, 32 q / 8 kv heads, d128, batch 64 with
+             context lengths U[512, 8192] (seeded); KV-head groups sharded
+             across ranks (strong scaling, no collective).
+  long_ctx   (config 5) 32 layers, 32 q / 8 kv heads, d128, one sequence of
+             131072 cached tokens sharded by token blocks; per layer each rank
+             emits (m, l, o) triples, one NCCL all-gather, LSE merge (strong).
+  prefill_05b (config 3) alone.
+
+Decode inputs exceed L2 (no flush needed); the prefill working set fits in
+L2, so a 256 MiB buffer is rewritten before each timed prefill call.
 
 --impl reference: the reference's attention (the CPU oracle restating
-packages/three-llm/src/runtime/math.ts causalAttention) on the host cores,
-all threads, on a bounded sample of the same workload.
+packages/three-llm/src/runtime/math.ts causalAttention) on all host threads,
+on a bounded sample of the chosen workload.
 """
 import argparse
-import ctypes
+import datetime
 import json
 import os
 import statistics
@@ -33,6 +41,11 @@ if str(ROOT) not in sys.path:
 
 METRIC = "decode attn GB/s (%HBM) + tok/s @1/2/4/8 B200; prefill attn TFLOP/s"
 
+DECODE_1B = dict(Hq=32, Hk=8, D=64, T=4096, layers=16, theta=500000.0, batch=64)
+RAGGED_8B = dict(Hq=32, Hk=8, D=128, layers=32, theta=500000.0, batch=64, lo=512, hi=8192)
+LONG_CTX = dict(Hq=32, Hk=8, D=128, T=131072, layers=32, theta=500000.0, batch=1)
+PREFILL_05B = dict(Hq=14, Hk=2, D=64, S=2048, B=4, T=4096, theta=1e6)
+
 
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
@@ -42,22 +55,14 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-# ---------------------------------------------------------------- workload definitions
-DECODE_1B = dict(name="decode_1b", Hq=32, Hk=8, D=64, T=4096, layers=16, theta=500000.0)
+def decode_seq_bytes(T1, Hq, Hk, D):
+    """Algorithmic HBM bytes of one sequence's decode in one layer: K and V of the
+    T1 attended tokens read, Q read and O written, the new K/V read and appended."""
+    return 2 * T1 * Hk * D * 2 + 2 * Hq * D * 2 + 2 * Hk * D * 2
 
 
-def decode_bytes_per_seq_layer(w):
-    """Algorithmic HBM bytes of one sequence's decode in one layer: the K and V of
-    T+1 tokens read, Q read and O written, the new K/V read and appended."""
-    T1 = w["T"] + 1
-    return 2 * T1 * w["Hk"] * w["D"] * 2 + 2 * w["Hq"] * w["D"] * 2 + 2 * w["Hk"] * w["D"] * 2
-
-
-def decode_flops_per_seq_layer(w):
-    return 4 * (w["T"] + 1) * w["D"] * w["Hq"]
-
-
-PREFILL_05B = dict(name="prefill_05b", Hq=14, Hk=2, D=64, S=2048, B=4, T=4096, theta=1e6)
+def ragged_lengths(w):
+    return np.random.default_rng(0).integers(w["lo"], w["hi"] + 1, size=w["batch"])
 
 
 def prefill_causal_flops(w):
@@ -67,7 +72,7 @@ def prefill_causal_flops(w):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples SM clock and throttle reasons with NVML while the timed region runs."""
+    """Samples SM clock and throttle reasons with NVML (read-only) while the timed region runs."""
 
     def __init__(self, index):
         self.index = index
@@ -84,12 +89,8 @@ class ClockSampler:
             pynvml.nvmlInit()
             h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
-            names = {
-                "hw_slowdown": getattr(pynvml, "nvmlClocksThrottleReasonHwSlowdown", 0x8),
-                "hw_thermal_slowdown": getattr(pynvml, "nvmlClocksThrottleReasonHwThermalSlowdown", 0x40),
-                "sw_thermal_slowdown": getattr(pynvml, "nvmlClocksThrottleReasonSwThermalSlowdown", 0x20),
-                "sw_power_cap": getattr(pynvml, "nvmlClocksThrottleReasonSwPowerCap", 0x4),
-            }
+            names = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+                     "sw_power_cap": 0x4}
 
             def run():
                 while not self._stop.is_set():
@@ -119,127 +120,191 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-# ---------------------------------------------------------------- our arm
-def fill_cache_random(pkg, layer, gen, torch):
+def cache_tensor(torch, ptr, numel, device):
+    class _Arr:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<f2", "data": (ptr, False), "version": 3}
+
+    return torch.as_tensor(_Arr(), device=device)
+
+
+def fill_cache_random(layer, gen, torch):
     """Fill a layer's whole fp16 cache with N(0,1) values (stand-in for post-RoPE keys / values)."""
     v = layer.cache_view()
     n = layer.maxBatch * layer.kvHeadCount * layer.maxTokens * layer.headDim
-
-    class _Arr:
-        def __init__(self, ptr):
-            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f2", "data": (ptr, False), "version": 3}
-
     for ptr in (v.key, v.value):
-        t = torch.as_tensor(_Arr(ptr), device=layer.device)
-        t.normal_(generator=gen)
+        cache_tensor(torch, ptr, n, layer.device).normal_(generator=gen)
 
 
-def run_decode(args, torch, rank, world, device):
-    import __graft_entry__ as ge
+# ---------------------------------------------------------------- workloads (our arm)
+class Decode1B:
+    """Config 2. step() launches one step (all layers) on the current stream;
+    e2e_step() does the same through pinned host buffers."""
 
-    pkg = ge.load_package()
-    w = dict(DECODE_1B)
-    B, L, T = args.batch, w["layers"], w["T"]
-    Hq, Hk, D = w["Hq"], w["Hk"], w["D"]
-    row = (Hq + 2 * Hk) * D
-    gen = torch.Generator(device=device)
-    gen.manual_seed(1234 + rank)
-    layers = []
-    for _ in range(L):
-        layer = pkg.CUDAAttention(None, Hq * D, Hq, T + 1, {"headDim": D, "kvHeadCount": Hk, "ropeTheta": w["theta"],
+    def __init__(self, pkg, torch, device, rank, world, args):
+        w = DECODE_1B
+        self.torch = torch
+        B, L, T, Hq, Hk, D = args.batch, w["layers"], w["T"], w["Hq"], w["Hk"], w["D"]
+        gen = torch.Generator(device=device)
+        gen.manual_seed(1234 + rank)
+        self.layers = []
+        for _ in range(L):
+            layer = pkg.CUDAAttention(None, Hq * D, Hq, T + 1, {"headDim": D, "kvHeadCount": Hk, "ropeTheta": w["theta"],
+                                                                "maxBatch": B, "dtype": torch.float16})
+            fill_cache_random(layer, gen, torch)
+            self.layers.append(layer)
+        self.qkv = torch.randn(L, B, (Hq + 2 * Hk) * D, generator=gen, device=device).half()
+        self.pos = torch.full((B,), T, dtype=torch.int32, device=device)
+        self.outs = torch.empty(L, B, Hq * D, dtype=torch.float16, device=device)
+        self.bytes_per_step = L * B * decode_seq_bytes(T + 1, Hq, Hk, D)
+        self.bytes_per_launch = B * decode_seq_bytes(T + 1, Hq, Hk, D)
+        self.tokens_per_step = B
+        self.launches_per_step = L
+        self.kernel = "decode_fast_kernel<64,half>"
+        self.config = {"workload": "decode_1b (config 2): 16 layers x 32q/8kv heads x d64, fp16 KV, 4096 cached + 1 "
+                                   "new, theta 5e5", "batch_per_gpu": B, "global_batch": B * world,
+                       "parallelism": f"batch-sharded x{world}",
+                       "l2": "inputs (8.6 GB of cache per step per GPU) larger than L2; no flush"}
+        self.scaling = "weak"
+
+    def step(self, record=None):
+        for i, layer in enumerate(self.layers):
+            if record:
+                record[0]()
+            layer.decode(self.qkv[i], self.pos, out=self.outs[i])
+            if record:
+                record[1]()
+
+    def e2e_setup(self):
+        t = self.torch
+        self.qkv_host = self.qkv.cpu().pin_memory()
+        self.pos_host = self.pos.cpu().pin_memory()
+        self.out_host = t.empty(self.outs.shape, dtype=t.float16).pin_memory()
+        self.qkv_dev = t.empty_like(self.qkv)
+        self.pos_dev = t.empty_like(self.pos)
+        self.h2d = self.qkv.numel() * 2 + self.pos.numel() * 4
+        self.d2h = self.outs.numel() * 2
+
+    def e2e_step(self):
+        self.qkv_dev.copy_(self.qkv_host, non_blocking=True)
+        self.pos_dev.copy_(self.pos_host, non_blocking=True)
+        for i, layer in enumerate(self.layers):
+            layer.decode(self.qkv_dev[i], self.pos_dev, out=self.outs[i])
+        self.out_host.copy_(self.outs, non_blocking=True)
+
+    def close(self):
+        for layer in self.layers:
+            layer.close()
+
+
+class Ragged8B(Decode1B):
+    """Config 4, sharded by KV-head group (each rank: its kv heads of every sequence)."""
+
+    def __init__(self, pkg, torch, device, rank, world, args):
+        from three_llm_b200 import sharding
+
+        w = RAGGED_8B
+        self.torch = torch
+        B, L, Hq, Hk, D = w["batch"], w["layers"], w["Hq"], w["Hk"], w["D"]
+        sh = sharding.head_shard(Hq, Hk, world, rank)
+        hq, hk = sh.q_count, sh.kv_count
+        lens = ragged_lengths(w)
+        T = int(lens.max()) + 1
+        gen = torch.Generator(device=device)
+        gen.manual_seed(77 + rank)
+        self.layers = []
+        for _ in range(L):
+            layer = pkg.CUDAAttention(None, hq * D, hq, T, {"headDim": D, "kvHeadCount": hk, "ropeTheta": w["theta"],
                                                             "maxBatch": B, "dtype": torch.float16})
-        fill_cache_random(pkg, layer, gen, torch)
-        layers.append(layer)
-    qkv = torch.randn(L, B, row, generator=gen, device=device).half()
-    positions = torch.full((B,), T, dtype=torch.int32, device=device)
-    outs = torch.empty(L, B, Hq * D, dtype=torch.float16, device=device)
-    stream = torch.cuda.current_stream()
-
-    def step():
-        for i in range(L):
-            layers[i].decode(qkv[i], positions, out=outs[i])
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    # per-launch events on the launching stream give the kernel's average duration
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps * L)]
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index) as clk:
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_push("timed")
-        start.record(stream)
-        k = 0
-        for _ in range(args.steps):
-            for i in range(L):
-                ev[k][0].record(stream)
-                layers[i].decode(qkv[i], positions, out=outs[i])
-                ev[k][1].record(stream)
-                k += 1
-        stop.record(stream)
-        torch.cuda.nvtx.range_pop()
-        torch.cuda.synchronize()
-    elapsed_ms = start.elapsed_time(stop)
-    launch_ms = [a.elapsed_time(b) for a, b in ev]
-    err = layers[0].context.error()
-    if err != 0:
-        raise RuntimeError(f"device reported status {err}")
-
-    # end to end through the public API: host (pinned) qkv in, outputs back to the host
-    qkv_host = qkv.cpu().pin_memory()
-    out_host = torch.empty(L, B, Hq * D, dtype=torch.float16).pin_memory()
-    pos_host = positions.cpu().pin_memory()
-    qkv_dev = torch.empty_like(qkv)
-    pos_dev = torch.empty_like(positions)
-
-    def e2e_step():
-        qkv_dev.copy_(qkv_host, non_blocking=True)
-        pos_dev.copy_(pos_host, non_blocking=True)
-        for i in range(L):
-            layers[i].decode(qkv_dev[i], pos_dev, out=outs[i])
-        out_host.copy_(outs, non_blocking=True)
-
-    for _ in range(max(1, args.warmup)):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-
-    bytes_per_launch = B * decode_bytes_per_seq_layer(w)
-    res = dict(elapsed_ms=elapsed_ms, e2e_ms=e2e_ms, launch_ms=float(np.mean(launch_ms)),
-               bytes_per_step=bytes_per_launch * L, bytes_per_launch=bytes_per_launch,
-               flops_per_step=B * L * decode_flops_per_seq_layer(w), tokens_per_step=B,
-               h2d=qkv.numel() * 2 + positions.numel() * 4, d2h=outs.numel() * 2, launches=args.steps * L,
-               clocks=clk.summary())
-    for layer in layers:
-        layer.close()
-    return res
+            fill_cache_random(layer, gen, torch)
+            self.layers.append(layer)
+        self.qkv = torch.randn(L, B, (hq + 2 * hk) * D, generator=gen, device=device).half()
+        self.pos = torch.from_numpy(lens.astype(np.int32)).to(device)
+        self.outs = torch.empty(L, B, hq * D, dtype=torch.float16, device=device)
+        per_layer = sum(decode_seq_bytes(int(t) + 1, hq, hk, D) for t in lens)
+        self.bytes_per_step = L * per_layer
+        self.bytes_per_launch = per_layer
+        self.tokens_per_step = B / world  # a rank computes its heads of every sequence
+        self.launches_per_step = L
+        self.kernel = "decode_fast_kernel<128,half>"
+        self.config = {"workload": "ragged_8b (config 4): 32 layers x 32q/8kv heads x d128, fp16 KV, batch 64, "
+                                   "context U[512, 8192] (seed 0), theta 5e5", "global_batch": B,
+                       "parallelism": f"kv-head groups x{world} ({hk} kv / {hq} q heads per GPU)",
+                       "l2": "inputs larger than L2; no flush"}
+        self.scaling = "strong"
 
 
-def run_prefill(args, torch, device):
+class LongCtx:
+    """Config 5, sharded by token blocks with an NCCL all-gather + LSE merge per layer."""
+
+    def __init__(self, pkg, torch, device, rank, world, args):
+        from three_llm_b200 import sharding
+
+        w = LONG_CTX
+        self.torch = torch
+        L, T, Hq, Hk, D = w["layers"], w["T"], w["Hq"], w["Hk"], w["D"]
+        gen = torch.Generator(device=device)
+        gen.manual_seed(5 + rank)
+        self.shards = []
+        for _ in range(L):
+            s = sharding.SequenceShardedDecode(Hq, Hk, D, T, rank, world, {"ropeTheta": w["theta"]})
+            fill_cache_random(s.layer, gen, torch)
+            self.shards.append(s)
+        self.layers = [s.layer for s in self.shards]
+        g0 = torch.Generator(device=device)
+        g0.manual_seed(5)  # identical queries on every rank
+        self.qkv = torch.randn(L, 1, (Hq + 2 * Hk) * D, generator=g0, device=device).half()
+        self.pos = torch.full((1,), T, dtype=torch.int32, device=device)
+        local = self.shards[0].shard.tokens + (1 if self.shards[0].shard.owns_next else 0)
+        self.bytes_per_step = L * decode_seq_bytes(T + 1, Hq, Hk, D) / world  # this rank's share
+        self.bytes_per_launch = decode_seq_bytes(local, Hq, Hk, D)
+        self.tokens_per_step = 1 / world
+        self.launches_per_step = 2 * L
+        self.kernel = "decode_fast_kernel<128,half> partial + NCCL all-gather + combine_lse_kernel"
+        self.config = {"workload": "long_ctx (config 5): 32 layers x 32q/8kv heads x d128, one sequence, 131072 "
+                                   "cached tokens + 1 new, fp16 KV, theta 5e5", "global_batch": 1,
+                       "parallelism": f"sequence blocks x{world}, NCCL all-gather of (m,l,o) + LSE merge per layer",
+                       "l2": "inputs larger than L2; no flush"}
+        self.scaling = "strong"
+        self.outs = torch.empty(L, 1, Hq * D, dtype=torch.float16, device=device)
+
+    def step(self, record=None):
+        for i, s in enumerate(self.shards):
+            if record:
+                record[0]()
+            self.outs[i].copy_(s.step(self.qkv[i], self.pos))
+            if record:
+                record[1]()
+
+    def e2e_setup(self):
+        t = self.torch
+        self.qkv_host = self.qkv.cpu().pin_memory()
+        self.out_host = t.empty(self.outs.shape, dtype=t.float16).pin_memory()
+        self.qkv_dev = t.empty_like(self.qkv)
+        self.h2d = self.qkv.numel() * 2
+        self.d2h = self.outs.numel() * 2
+
+    def e2e_step(self):
+        self.qkv_dev.copy_(self.qkv_host, non_blocking=True)
+        for i, s in enumerate(self.shards):
+            self.outs[i].copy_(s.step(self.qkv_dev[i], self.pos))
+        self.out_host.copy_(self.outs, non_blocking=True)
+
+    def close(self):
+        for layer in self.layers:
+            layer.close()
+
+
+def run_prefill(pkg, torch, device, args):
     """causal prefill of 4 x 2048 tokens, 14 q / 2 kv heads, d64,
-    RoPE theta 1e6 applied in-kernel, K/V written into a 4096-slot cache. The
-    working set fits in L2, so a 256 MiB buffer is rewritten before every timed call."""
-    import __graft_entry__ as ge
-
-    pkg = ge.load_package()
+    RoPE theta 1e6 applied in-kernel, K/V written into a 4096-slot cache."""
     w = PREFILL_05B
     B, S, Hq, Hk, D = w["B"], w["S"], w["Hq"], w["Hk"], w["D"]
-    row = (Hq + 2 * Hk) * D
     gen = torch.Generator(device=device)
     gen.manual_seed(99)
     layer = pkg.CUDAAttention(None, Hq * D, Hq, w["T"], {"headDim": D, "kvHeadCount": Hk, "ropeTheta": w["theta"],
                                                          "maxBatch": B, "dtype": torch.float16})
-    qkv = torch.randn(B, S, row, generator=gen, device=device).half()
+    qkv = torch.randn(B, S, (Hq + 2 * Hk) * D, generator=gen, device=device).half()
     start = torch.zeros(B, dtype=torch.int32, device=device)
     out = torch.empty(B, S, Hq * D, dtype=torch.float16, device=device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
@@ -258,38 +323,95 @@ def run_prefill(args, torch, device):
     torch.cuda.synchronize()
     ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
     err = layer.context.error()
+    layer.close()
     if err != 0:
         raise RuntimeError(f"device reported status {err}")
     flops = prefill_causal_flops(w)
-    layer.close()
     return dict(ms=ms, flops=flops, tflops=flops / (ms * 1e-3) / 1e12, launches=2 * args.steps)
 
 
+WORKLOADS = {"decode_1b": Decode1B, "ragged_8b": Ragged8B, "long_ctx": LongCtx}
+
+
+def timed(torch, wl, args, world, device):
+    """Warm-up, then K timed steps between barrier + synchronize, with per-layer
+    events on the launching stream; then K end-to-end steps through host buffers."""
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps * len(wl.layers))]
+    k = [0]
+
+    def rec_start():
+        ev[k[0]][0].record(stream)
+
+    def rec_stop():
+        ev[k[0]][1].record(stream)
+        k[0] += 1
+
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clk:
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("timed")
+        start.record(stream)
+        for _ in range(args.steps):
+            wl.step((rec_start, rec_stop))
+        stop.record(stream)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+    elapsed = start.elapsed_time(stop)
+    per_launch = float(np.mean([a.elapsed_time(b) for a, b in ev[:k[0]]]))
+    err = wl.layers[0].context.error()
+    if err != 0:
+        raise RuntimeError(f"device reported status {err}")
+    wl.e2e_setup()
+    for _ in range(max(1, args.warmup)):
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        wl.e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return elapsed, e0.elapsed_time(e1), per_launch, clk.summary()
+
+
 # ---------------------------------------------------------------- CPU legs (oracle)
-def cpu_decode_sample(threads, layers_in_sample=1, batch=None, heads=None):
-    """Time the reference's causalAttention attention loops (the oracle) on a bounded
-    sample of the decode workload: `batch` sequences x `heads` query heads of one
-    layer at 4096 cached tokens. Returns (GB/s of algorithmic bytes, seconds, description)."""
+def cpu_decode_sample(threads, workload="decode_1b", batch=4, heads=None):
+    """Time the oracle's attention loops (the reference's causalAttention restated) on a
+    bounded sample of a decode workload. Returns (GB/s of algorithmic bytes, seconds, description)."""
     from oracle import oracle
 
-    w = DECODE_1B
-    Hq, Hk, D, T = w["Hq"], w["Hk"], w["D"], w["T"]
-    B = batch or 1
+    if workload == "ragged_8b":
+        w = RAGGED_8B
+        T = int(np.mean(ragged_lengths(w)))
+    elif workload == "long_ctx":
+        w = LONG_CTX
+        T = 16384  # a bounded slice of the 131072-token context
+    else:
+        w = DECODE_1B
+        T = w["T"]
+    Hq, Hk, D = w["Hq"], w["Hk"], w["D"]
     heads = heads or Hq
     rng = np.random.default_rng(0)
-    kc = rng.standard_normal((B, T + 1, Hk * D), dtype=np.float32)
-    vc = rng.standard_normal((B, T + 1, Hk * D), dtype=np.float32)
-    q = rng.standard_normal((B, Hq * D), dtype=np.float32)
-    pos = np.full(B, T, np.int32)
+    kc = rng.standard_normal((batch, T + 1, Hk * D), dtype=np.float32)
+    vc = rng.standard_normal((batch, T + 1, Hk * D), dtype=np.float32)
+    q = rng.standard_normal((batch, Hq * D), dtype=np.float32)
+    pos = np.full(batch, T, np.int32)
     opts = dict(head_count=Hq, kv_head_count=Hk, head_dim=D)
     oracle.attend_heads(q, pos, kc, vc, 0, min(heads, 2), threads=threads, **opts)  # warm
     t0 = time.perf_counter()
-    for _ in range(layers_in_sample):
-        oracle.attend_heads(q, pos, kc, vc, 0, heads, threads=threads, **opts)
+    oracle.attend_heads(q, pos, kc, vc, 0, heads, threads=threads, **opts)
     dt = time.perf_counter() - t0
-    frac = heads / Hq
-    nbytes = layers_in_sample * B * decode_bytes_per_seq_layer(w) * frac
-    desc = f"{B} seq x {heads}/{Hq} q heads x {layers_in_sample} layer(s) at 4096 cached tokens, fp32 (oracle)"
+    nbytes = batch * decode_seq_bytes(T + 1, Hq, Hk, D) * heads / Hq
+    desc = f"{batch} seq x {heads}/{Hq} q heads x 1 layer at {T} cached tokens, fp32 (oracle)"
     return nbytes / dt / 1e9, dt, desc
 
 
@@ -297,20 +419,17 @@ def run_reference(args):
     from oracle import oracle
 
     threads = oracle.cpu_count()
-    vals = []
-    for _ in range(args.warmup):
-        cpu_decode_sample(threads, batch=args.ref_batch)
-    for _ in range(args.steps):
-        gbs, dt, desc = cpu_decode_sample(threads, batch=args.ref_batch)
-        vals.append((gbs, dt))
+    batch = args.ref_batch if args.workload == "decode_1b" else (8 if args.workload == "ragged_8b" else 1)
+    cpu_decode_sample(threads, args.workload, batch=min(batch, 2))  # warm
+    vals = [cpu_decode_sample(threads, args.workload, batch=batch) for _ in range(args.steps)]
     gbs = statistics.median(v[0] for v in vals)
     dt = statistics.median(v[1] for v in vals)
+    desc = vals[0][2]
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "decode_1b: 16 layers x 32q/8kv heads x d64, 4096 cached + 1, batch 64, theta 5e5",
-                   "sample": desc},
+        "config": {"workload": args.workload, "sample": desc},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -324,7 +443,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--workload", default="decode_1b", choices=list(WORKLOADS) + ["prefill_05b"])
+    ap.add_argument("--batch", type=int, default=DECODE_1B["batch"], help="decode_1b sequences per GPU")
     ap.add_argument("--ref-batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
@@ -334,65 +454,76 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         if rank == 0:
-            if args.steps > 3:
-                args.steps = 3  # each reference step is a multi-second CPU sample
+            args.steps = min(args.steps, 3)  # each reference step is a multi-second CPU sample
             run_reference(args)
         return
 
     import torch
 
+    import __graft_entry__ as ge
+
+    pkg = ge.load_package()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world > 1:
-        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    hbm, tc, src = peaks()
+    if args.workload == "prefill_05b":
+        pre = run_prefill(pkg, torch, device, args)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": round(pre["tflops"], 2), "unit": "TFLOP/s", "n_gpus": 1,
+                              "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(pre["ms"], 5),
+                              "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+                              "data": "synthetic", "config": {"workload": "prefill_05b (config 3)"},
+                              "roofline": {"bound": "tensor", "achieved": round(pre["tflops"], 2), "peak": tc,
+                                           "unit": "TFLOP/s", "frac": round(pre["tflops"] / tc, 4), "traffic": None,
+                                           "peak_source": src}, "gpu_launches": pre["launches"]}), flush=True)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return
 
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=device)
-    res = run_decode(args, torch, rank, world, device)
-    pre = None if args.no_prefill else run_prefill(args, torch, device)
-    t = torch.tensor([res["elapsed_ms"], res["e2e_ms"]], dtype=torch.float64, device=device)
+    wl = WORKLOADS[args.workload](pkg, torch, device, rank, world, args)
+    elapsed, e2e_ms, per_launch, clocks = timed(torch, wl, args, world, device)
+    pre = run_prefill(pkg, torch, device, args) if (args.workload == "decode_1b" and not args.no_prefill) else None
+    t = torch.tensor([elapsed, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    elapsed_ms, e2e_ms = float(t[0]), float(t[1])
-    hbm, tc, src = peaks()
+    elapsed, e2e_ms = float(t[0]), float(t[1])
     if rank == 0:
-        ms = elapsed_ms / args.steps
-        total_bytes = res["bytes_per_step"] * args.steps * world
-        gbs = total_bytes / (elapsed_ms * 1e-3) / 1e9
+        ms = elapsed / args.steps
+        total_bytes = wl.bytes_per_step * args.steps * world
+        gbs = total_bytes / (elapsed * 1e-3) / 1e9
         e2e_gbs = total_bytes / (e2e_ms * 1e-3) / 1e9
-        achieved = res["bytes_per_launch"] / (res["launch_ms"] * 1e-3) / 1e9
+        achieved = wl.bytes_per_launch / (per_launch * 1e-3) / 1e9
+        tokens = wl.tokens_per_step * world
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": wl.scaling,
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic (seeded N(0,1) fp16 cache and qkv)",
-            "config": {"workload": "decode_1b: 16 layers x 32q/8kv heads x d64, fp16 KV, 4096 cached + 1 new, "
-                                   "theta 5e5", "batch_per_gpu": args.batch, "global_batch": args.batch * world,
-                       "parallelism": f"batch-sharded x{world}",
-                       "l2": "inputs (8.6 GB cache per step per GPU) larger than L2; no flush"},
-            "tok_s": round(args.batch * world / (ms * 1e-3), 1),
-            "hbm_frac": round(gbs / world / hbm, 4),
+            "config": wl.config, "tok_s": round(tokens / (ms * 1e-3), 1), "hbm_frac": round(gbs / world / hbm, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "traffic": None,
-                         "kernel": "decode_fast_kernel<64,half>", "peak_source": src,
-                         "launch_ms": round(res["launch_ms"], 5)},
-            "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": res["h2d"],
-                    "d2h_bytes_per_step": res["d2h"], "ms_per_step": round(e2e_ms / args.steps, 4)},
-            "gpu_launches": res["launches"] + (pre["launches"] if pre else 0),
-            "clocks": res["clocks"],
+                         "frac": round(achieved / hbm, 4), "traffic": None, "kernel": wl.kernel,
+                         "peak_source": src, "launch_ms": round(per_launch, 5)},
+            "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": wl.h2d,
+                    "d2h_bytes_per_step": wl.d2h, "ms_per_step": round(e2e_ms / args.steps, 4)},
+            "gpu_launches": int(args.steps * wl.launches_per_step + (pre["launches"] if pre else 0)),
+            "clocks": clocks,
         }
         if pre:
-            line["prefill"] = {"workload": "prefill_05b: 4 x 2048 tokens, 14q/2kv heads, d64, causal, RoPE theta 1e6 "
-                                           "in-kernel, K/V appended to a 4096-slot cache; L2 flushed per call",
-                               "tflops": round(pre["tflops"], 2), "ms": round(pre["ms"], 5),
-                               "causal_gflop": round(pre["flops"] / 1e9, 3),
-                               "frac": round(pre["tflops"] / tc, 4), "peak_tflops": tc, "peak_source": src,
-                               "kernels": "rope_append_kernel + prefill_tc_kernel<64,half>"}
+            line["prefill"] = {"workload": "prefill_05b (config 3): 4 x 2048 tokens, 14q/2kv heads, d64, causal, "
+                                           "RoPE theta 1e6 in-kernel, K/V appended to a 4096-slot cache; L2 flushed "
+                                           "per call", "tflops": round(pre["tflops"], 2), "ms": round(pre["ms"], 5),
+                               "causal_gflop": round(pre["flops"] / 1e9, 3), "frac": round(pre["tflops"] / tc, 4),
+                               "peak_tflops": tc, "peak_source": src,
+                               "kernels": "rope_append_warp_kernel + prefill_tc_kernel<64,half>"}
         if not args.no_cpu_baseline:
-            gb, dt, desc = cpu_decode_sample(1, batch=4, heads=32)
+            gb, dt, desc = cpu_decode_sample(1, args.workload, batch=4 if args.workload == "decode_1b" else 1)
             line["cpu_baseline"] = {"value": round(gb, 4), "unit": "GB/s", "cores": 1, "kind": "port",
                                     "sample": desc + f" ({dt:.2f} s)"}
         print(json.dumps(line), flush=True)
+    wl.close()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -48,11 +48,13 @@ struct PCfg {
   static constexpr int kPB = D == 64 ? 2 : 1;           // P buffers
   static constexpr int kPBytes = 2 * kBoxBytes;        // [128 rows][128 fp16]
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kTileBytes;           // 2 stages
-  static constexpr int kV = kK + 2 * kTileBytes;       // 2 stages
-  static constexpr int kP = kV + 2 * kTileBytes;
+  static constexpr int kST = D == 64 ? 3 : 2;          // K/V ring stages
+  static constexpr int kK = kQ + kTileBytes;
+  static constexpr int kV = kK + kST * kTileBytes;
+  static constexpr int kP = kV + kST * kTileBytes;
   static constexpr int kBar = kP + kPB * kPBytes;
-  static constexpr int kNumBars = 1 + 2 + 2 + 2 + 2 + 2 + 2 * kPB + 2 + 2;
+  // q_full, k_full/v_full/k_empty/v_empty [kST], s_full/s_free [2], p_full/p_free [kPB], o_full/o_free [2]
+  static constexpr int kNumBars = 1 + 4 * kST + 4 + 2 * kPB + 4;
   static constexpr int kRed = kBar + kNumBars * 8 + 16;      // [2][kNW][128] row-max partials
   static constexpr int kSmem = kRed + 2 * kNW * 128 * 4 + 1024;
   static constexpr uint32_t kTmemCols = 512;           // S 2x128 + O 2xD
@@ -148,11 +150,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* v_full = bars + 3;
-  uint64_t* kv_empty = bars + 5;
-  uint64_t* s_full = bars + 7;
-  uint64_t* s_free = bars + 9;
-  uint64_t* p_full = bars + 11;
+  uint64_t* v_full = k_full + C::kST;
+  uint64_t* k_empty = v_full + C::kST;
+  uint64_t* v_empty = k_empty + C::kST;
+  uint64_t* s_full = v_empty + C::kST;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
   uint64_t* p_free = p_full + C::kPB;
   uint64_t* o_full = p_free + C::kPB;
   uint64_t* o_free = o_full + 2;
@@ -175,10 +178,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 
   if (tid == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::kST; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kSoftmaxThreads);
       mbar_init(&o_full[i], 1);
@@ -218,23 +224,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       for (int x = 0; x < C::kBoxes; ++x)
         tma_load_3d(smem + C::kQ + x * C::kBoxBytes, &p.tm_q, q_full, x * 64, row0, b * p.Hq + h);
       for (int n = 0; n < ntiles; ++n) {
-        const int st = n & 1;
-        wait(&kv_empty[st], ((n >> 1) & 1) ^ 1);
-        if (*abort_flag) continue;
+        const int st = n % C::kST;
+        const uint32_t ph = ((n / C::kST) & 1) ^ 1;
         const int y = (j0 + n) * kCols, z = b * p.Hk + kvh;
-        mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
+        wait(&k_empty[st], ph);  // freed once S of the tile that used it completed
+        if (!*abort_flag) {
+          mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
 #pragma unroll
-        for (int x = 0; x < C::kBoxes; ++x)
-          tma_load_3d(smem + C::kK + st * C::kTileBytes + x * C::kBoxBytes, &p.tm_k, &k_full[st], x * 64, y, z);
-        mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
+          for (int x = 0; x < C::kBoxes; ++x)
+            tma_load_3d(smem + C::kK + st * C::kTileBytes + x * C::kBoxBytes, &p.tm_k, &k_full[st], x * 64, y, z);
+        }
+        wait(&v_empty[st], ph);  // freed once its P V completed
+        if (!*abort_flag) {
+          mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
 #pragma unroll
-        for (int x = 0; x < C::kBoxes; ++x)
-          tma_load_3d(smem + C::kV + st * C::kTileBytes + x * C::kBoxBytes, &p.tm_v, &v_full[st], x * 64, y, z);
+          for (int x = 0; x < C::kBoxes; ++x)
+            tma_load_3d(smem + C::kV + st * C::kTileBytes + x * C::kBoxBytes, &p.tm_v, &v_full[st], x * 64, y, z);
+        }
       }
       // no copies may be in flight when the CTA exits
-      for (int n = max(0, ntiles - 2); n < ntiles; ++n) {
-        wait(&k_full[n & 1], (n >> 1) & 1);
-        wait(&v_full[n & 1], (n >> 1) & 1);
+      for (int n = max(0, ntiles - C::kST); n < ntiles; ++n) {
+        wait(&k_full[n % C::kST], (n / C::kST) & 1);
+        wait(&v_full[n % C::kST], (n / C::kST) & 1);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -246,8 +257,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       wait(q_full, 0);
       for (int n = 0; n <= ntiles; ++n) {
         if (n < ntiles) {
-          const int st = n & 1, sb = n & 1;
-          wait(&k_full[st], (n >> 1) & 1);
+          const int st = n % C::kST, sb = n & 1;
+          wait(&k_full[st], (n / C::kST) & 1);
           wait(&s_free[sb], ((n >> 1) & 1) ^ 1);
           tc_fence_after();
           const uint32_t k_base = smem_u32(smem + C::kK + st * C::kTileBytes);
@@ -260,11 +271,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             }
           }
           mma_commit(&s_full[sb]);
+          mma_commit(&k_empty[st]);
         }
         if (n >= 1) {
-          const int q = n - 1, st = q & 1, ob = q & 1, pb = q % C::kPB;
+          const int q = n - 1, st = q % C::kST, ob = q & 1, pb = q % C::kPB;
           wait(&p_full[pb], (q / C::kPB) & 1);
-          wait(&v_full[st], (q >> 1) & 1);
+          wait(&v_full[st], (q / C::kST) & 1);
           wait(&o_free[ob], ((q >> 1) & 1) ^ 1);
           tc_fence_after();
           const uint32_t p_base = smem_u32(smem + C::kP + pb * C::kPBytes);
@@ -276,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
                       sdesc(v_base + kk * 2048, C::kBoxBytes, 1024), kIdO, kk > 0 ? 1u : 0u);
           }
           mma_commit(&o_full[ob]);
-          mma_commit(&kv_empty[st]);
+          mma_commit(&v_empty[st]);
           mma_commit(&p_free[pb]);
         }
       }
