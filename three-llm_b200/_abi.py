@@ -5,10 +5,12 @@ N-API addon shown in INTEGRATION.md does the same in C++). There is no CPU
 fallback: loading fails loudly if the CUDA library has not been built.
 """
 import ctypes
+import os
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-LIB_PATH = HERE / "libtla.so"
+# TLA_LIBRARY selects another build of the same library (e.g. a tuning variant).
+LIB_PATH = Path(os.environ.get("TLA_LIBRARY", HERE / "libtla.so"))
 
 TLA_OK = 0
 STATUS = {

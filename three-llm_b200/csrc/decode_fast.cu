@@ -39,15 +39,25 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxBatch = 1024;      // prefix table in shared memory
 
+// Pipeline depth per head_dim: at 2 resident CTAs per SM a 4-stage (D=64) or
+// 2-stage (D=128) ring keeps 64-128 KB of K/V in flight per SM.
+#ifndef TLA_DECODE_STAGES_D64
+#define TLA_DECODE_STAGES_D64 4
+#endif
+#ifndef TLA_DECODE_STAGES_D128
+#define TLA_DECODE_STAGES_D128 2
+#endif
+
 template <int D>
 struct Cfg {
-  static constexpr int kStages = D == 64 ? 4 : 3;
-  static constexpr int kBoxes = D / 64;                      // 64-element TMA boxes per row
-  static constexpr int kBoxBytes = kTile * 128;              // one [64 tok][64 el] fp16 box
-  static constexpr int kTileBytes = kBoxes * kBoxBytes;      // K (or V) of one tile
+  static constexpr int kStages = D == 64 ? TLA_DECODE_STAGES_D64 : TLA_DECODE_STAGES_D128;
+  // A cache row of D fp16 is viewed as kHalves consecutive 128-byte rows, so a
+  // 64-token tile is one contiguous [kHalves * 64][64] box (16 KB for D=128).
+  static constexpr int kHalves = D / 64;
+  static constexpr int kTileBytes = kTile * kHalves * 128;   // K (or V) of one tile
   static constexpr int kStageBytes = 2 * kTileBytes;         // K + V
   static constexpr int kQPitch = D * 2 + 16;                 // padded row pitch of the Q tile
-  static constexpr int kMinBlocks = D == 64 ? 3 : 2;
+  static constexpr int kMinBlocks = 2;
 };
 
 struct DecodeParams {
@@ -62,6 +72,7 @@ struct DecodeParams {
   float* scratch;      // [grid][2][G][D + 2]
   int32_t* counters;   // [B * Hk], zero between launches
   int batch, slot_offset, local_tokens, append;
+  int defer_merge;  // 1: split pairs are merged by decode_merge_kernel instead of the last CTA
 };
 
 struct SmemLayout {
@@ -224,11 +235,8 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
           mbar_arrive_expect_tx(&full[s], C::kStageBytes);
           uint8_t* kst = stages + s * C::kStageBytes;
           const int y = lo + j * kTile, z = b * Hk + kvh;
-#pragma unroll
-          for (int x = 0; x < C::kBoxes; ++x) {
-            tma_load_3d(kst + x * C::kBoxBytes, &p.tmap_k, &full[s], x * 64, y, z);
-            tma_load_3d(kst + C::kTileBytes + x * C::kBoxBytes, &p.tmap_v, &full[s], x * 64, y, z);
-          }
+          tma_load_3d(kst, &p.tmap_k, &full[s], 0, y * C::kHalves, z);
+          tma_load_3d(kst + C::kTileBytes, &p.tmap_v, &full[s], 0, y * C::kHalves, z);
         }
         g += n;
       }
@@ -365,9 +373,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         const int r = slot_new - y0;
         if (r >= tok0 && r < tok0 + 16 && lane < D / 8) {
           const int box = lane >> 3, ch = lane & 7;
-          *reinterpret_cast<uint4*>(kst + box * C::kBoxBytes + sw128(r, ch)) =
+          *reinterpret_cast<uint4*>(kst + sw128(r * C::kHalves + box, ch)) =
               reinterpret_cast<const uint4*>(newkv)[lane];
-          *reinterpret_cast<uint4*>(vst + box * C::kBoxBytes + sw128(r, ch)) =
+          *reinterpret_cast<uint4*>(vst + sw128(r * C::kHalves + box, ch)) =
               reinterpret_cast<const uint4*>(newkv + D)[lane];
           wrote = true;
         }
@@ -381,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         const int tok = tok0 + (lane & 7) + ((lane >> 4) << 3);
         const int chunk = 2 * kk + ((lane >> 3) & 1);
         uint32_t r0, r1, r2, r3;
-        ldsm_x4(kbase + (chunk >> 3) * C::kBoxBytes + sw128(tok, chunk & 7), r0, r1, r2, r3);
+        ldsm_x4(kbase + sw128(tok * C::kHalves + (chunk >> 3), chunk & 7), r0, r1, r2, r3);
         mma_16816(acc[0], qa[kk], r0, r1);
         mma_16816(acc[1], qa[kk], r2, r3);
       }
@@ -443,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         const int tok = tok0 + (lane & 7) + (((lane >> 3) & 1) << 3);
         const int chunk = 2 * dd + (lane >> 4);
         uint32_t r0, r1, r2, r3;
-        ldsm_x4_t(vbase + (chunk >> 3) * C::kBoxBytes + sw128(tok, chunk & 7), r0, r1, r2, r3);
+        ldsm_x4_t(vbase + sw128(tok * C::kHalves + (chunk >> 3), chunk & 7), r0, r1, r2, r3);
         mma_16816(o[2 * dd], pa, r0, r1);
         mma_16816(o[2 * dd + 1], pa, r2, r3);
       }
@@ -521,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         static_cast<IO*>(p.out)[oi] = from_f32<IO>(val);
       }
     }
-    if (!whole) {
+    if (!whole && !p.defer_merge) {
       // ---- ticket: the CTA that completes the pair merges all its segments
       __threadfence();
       named_barrier_sync(1, 128);
@@ -532,32 +540,92 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       }
       named_barrier_sync(1, 128);
       if (flags[1]) {
+        // Merge every segment of this pair. The loads of different segments
+        // are independent, so the maxima and sums are block reductions and
+        // the output rows loop over segments without serial dependences.
         __threadfence();
         const long long pb = prefix[b] + static_cast<long long>(kvh) * tiles;
         const int c0 = cta_of(pb, total, grid), c1 = cta_of(pb + tiles - 1, total, grid);
-        for (int i = tid; i < G * (D + 2); i += 128) {
-          const int r = i / (D + 2), e = i - r * (D + 2);
-          float M = -INFINITY;
-          for (int c = c0; c <= c1; ++c) {
-            if (cta_begin(c + 1, total, grid) == cta_begin(c, total, grid)) continue;  // empty range
-            const int sl = cta_begin(c, total, grid) >= pb ? 0 : 1;
-            M = fmaxf(M, __ldcg(p.scratch + ((static_cast<size_t>(c) * 2 + sl) * G + r) * (D + 2)));
+        // Slot of each contributing CTA (-1: empty range), computed once; qf is
+        // free here and holds 16*D ints (the host keeps grid <= 16*D).
+        int* slot_of = reinterpret_cast<int*>(qf);
+        for (int c = c0 + tid; c <= c1; c += 128) {
+          const long long cb = cta_begin(c, total, grid);
+          slot_of[c - c0] = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
+        }
+        named_barrier_sync(1, 128);
+        auto seg = [&](int c) -> const float* {  // this pair's triple block in CTA c's scratch, or null
+          const int sl = slot_of[c - c0];
+          return sl < 0 ? nullptr : p.scratch + static_cast<size_t>(sl) * G * (D + 2);
+        };
+        float lm[16], ll[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          lm[r] = -INFINITY;
+          ll[r] = 0.f;
+        }
+        for (int c = c0 + tid; c <= c1; c += 128) {
+          const float* sp = seg(c);
+          if (sp == nullptr) continue;
+#pragma unroll
+          for (int r = 0; r < 16; ++r)
+            if (r < G) lm[r] = fmaxf(lm[r], __ldcg(sp + r * (D + 2)));
+        }
+        float* sred = red;                     // [4][G] maxima
+        float* sM = red + 8 * G;               // [G] merged maxima
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          if (r < G) {
+            float v = lm[r];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (lane == 0) sred[warp * G + r] = v;
           }
-          float v = 0.f, Lsum = 0.f;
-          for (int c = c0; c <= c1; ++c) {
-            if (cta_begin(c + 1, total, grid) == cta_begin(c, total, grid)) continue;
-            const int sl = cta_begin(c, total, grid) >= pb ? 0 : 1;
-            const float* pc = p.scratch + ((static_cast<size_t>(c) * 2 + sl) * G + r) * (D + 2);
-            const float w = ex2(__ldcg(pc) - M);
-            if (e >= 1) v += __ldcg(pc + e) * w;
-            if (e >= 2 && !p.partial_out) Lsum += __ldcg(pc + 1) * w;
+        }
+        named_barrier_sync(1, 128);
+        if (tid < G)
+          sM[tid] = fmaxf(fmaxf(sred[tid], sred[G + tid]), fmaxf(sred[2 * G + tid], sred[3 * G + tid]));
+        named_barrier_sync(1, 128);
+        for (int c = c0 + tid; c <= c1; c += 128) {
+          const float* sp = seg(c);
+          if (sp == nullptr) continue;
+#pragma unroll
+          for (int r = 0; r < 16; ++r)
+            if (r < G) ll[r] += __ldcg(sp + r * (D + 2) + 1) * ex2(__ldcg(sp + r * (D + 2)) - sM[r]);
+        }
+        float* ssum = red + 4 * G;             // [4][G] sums
+        float* sL = red + 9 * G;               // [G] merged sums
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          if (r < G) {
+            const float v = warp_sum(ll[r]);
+            if (lane == 0) ssum[warp * G + r] = v;
           }
-          if (e == 0) v = M;
+        }
+        named_barrier_sync(1, 128);
+        if (tid < G) sL[tid] = (ssum[tid] + ssum[G + tid]) + (ssum[2 * G + tid] + ssum[3 * G + tid]);
+        named_barrier_sync(1, 128);
+        for (int i = tid; i < G * D; i += 128) {
+          const int r = i / D, d = i - r * D;
+          const float M = sM[r];
+          float acc = 0.f;
+#pragma unroll 8
+          for (int c = c0; c <= c1; ++c) {
+            const float* sp = seg(c);
+            if (sp == nullptr) continue;
+            const float* row = sp + r * (D + 2);
+            acc += __ldcg(row + 2 + d) * ex2(__ldcg(row) - M);
+          }
+          const size_t hrow = static_cast<size_t>(b) * Hq + kvh * G + r;
           if (p.partial_out) {
-            p.partial_out[(static_cast<size_t>(b) * Hq + kvh * G + r) * (D + 2) + e] = v;
-          } else if (e >= 2) {
-            float val = v / Lsum;
-            const size_t oi = (static_cast<size_t>(b) * Hq + kvh * G + r) * D + (e - 2);
+            p.partial_out[hrow * (D + 2) + 2 + d] = acc;
+            if (d == 0) {
+              p.partial_out[hrow * (D + 2)] = M;
+              p.partial_out[hrow * (D + 2) + 1] = sL[r];
+            }
+          } else {
+            float val = acc / sL[r];
+            const size_t oi = hrow * D + d;
             if (p.gate) val = val * (1.f / (1.f + expf(-to_f32(static_cast<const IO*>(p.gate)[oi]))));
             static_cast<IO*>(p.out)[oi] = from_f32<IO>(val);
           }
@@ -570,10 +638,97 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
   }
 }
 
+// Deferred merge for pairs split across many CTAs (few, long sequences): one
+// block per (pair, query row), one thread per output element; the segment
+// maxima and sums are block reductions and each thread's loop over segments
+// issues independent loads. Pairs covered by a single CTA were written by the
+// decode kernel and are skipped.
+template <int D, typename IO>
+__global__ void __launch_bounds__(D) decode_merge_kernel(const __grid_constant__ DecodeParams p, int grid) {
+  __shared__ long long prefix[kMaxBatch + 1];
+  __shared__ float red[2][D / 32];
+  const LayerArgs& a = p.a;
+  const int G = a.G, Hk = a.Hk;
+  const int pair = blockIdx.x / G, r = blockIdx.x - pair * G;
+  const int b = pair / Hk, kvh = pair - b * Hk;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {  // the decode kernel's partition, recomputed (the batch is small on this path)
+    long long acc = 0;
+    for (int bb = 0; bb < p.batch; ++bb) {
+      prefix[bb] = acc;
+      const int pos = p.positions[bb];
+      int lo, hi;
+      seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
+      const bool ok = pos >= 0 && (p.partial_out != nullptr || pos < a.max_tokens) &&
+                      (!p.append || (pos - p.slot_offset >= 0 && pos - p.slot_offset < a.max_tokens &&
+                                     pos - p.slot_offset == hi));
+      acc += (ok && hi >= lo) ? static_cast<long long>((hi - lo + kTile) / kTile) * Hk : 0;
+    }
+    prefix[p.batch] = acc;
+  }
+  __syncthreads();
+  const long long total = prefix[p.batch];
+  const int tiles = static_cast<int>((prefix[b + 1] - prefix[b]) / Hk);
+  if (tiles == 0) return;
+  const long long pb = prefix[b] + static_cast<long long>(kvh) * tiles;
+  const int c0 = cta_of(pb, total, grid), c1 = cta_of(pb + tiles - 1, total, grid);
+  if (c0 == c1) return;  // one CTA held the whole pair
+  auto seg = [&](int c) -> const float* {
+    const long long cb = cta_begin(c, total, grid);
+    if (cta_begin(c + 1, total, grid) == cb) return nullptr;
+    return p.scratch + ((static_cast<size_t>(c) * 2 + (cb >= pb ? 0 : 1)) * G + r) * (D + 2);
+  };
+  float m = -INFINITY;
+  for (int c = c0 + tid; c <= c1; c += D) {
+    const float* sp = seg(c);
+    if (sp) m = fmaxf(m, sp[0]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[0][warp] = m;
+  __syncthreads();
+  float M = red[0][0];
+#pragma unroll
+  for (int w = 1; w < D / 32; ++w) M = fmaxf(M, red[0][w]);
+  float l = 0.f;
+  for (int c = c0 + tid; c <= c1; c += D) {
+    const float* sp = seg(c);
+    if (sp) l += sp[1] * ex2(sp[0] - M);
+  }
+  l = warp_sum(l);
+  if (lane == 0) red[1][warp] = l;
+  __syncthreads();
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < D / 32; ++w) L += red[1][w];
+  float acc = 0.f;
+#pragma unroll 8
+  for (int c = c0; c <= c1; ++c) {
+    const float* sp = seg(c);
+    if (sp) acc += sp[2 + tid] * ex2(sp[0] - M);
+  }
+  const size_t hrow = static_cast<size_t>(b) * a.Hq + kvh * G + r;
+  if (p.partial_out) {
+    p.partial_out[hrow * (D + 2) + 2 + tid] = acc;
+    if (tid == 0) {
+      p.partial_out[hrow * (D + 2)] = M;
+      p.partial_out[hrow * (D + 2) + 1] = L;
+    }
+  } else {
+    float val = acc / L;
+    const size_t oi = hrow * D + tid;
+    if (p.gate) val = val * (1.f / (1.f + expf(-to_f32(static_cast<const IO*>(p.gate)[oi]))));
+    static_cast<IO*>(p.out)[oi] = from_f32<IO>(val);
+  }
+}
+
 template <int D, typename IO, bool TWO>
 cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, cudaStream_t stream) {
   const SmemLayout s = smem_layout<D>(L->G, p.batch);
   decode_fast_kernel<D, IO, TWO><<<L->decode_grid, kThreads, s.total, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !p.defer_merge) return e;
+  decode_merge_kernel<D, IO><<<p.batch * L->Hk * L->G, D, 0, stream>>>(p, L->decode_grid);
   return cudaGetLastError();
 }
 
@@ -602,12 +757,12 @@ cudaError_t dispatch_launch(const tla_layer* L, const DecodeParams& p, cudaStrea
 }
 
 CUresult make_cache_map(const tla_layer* L, void* base, CUtensorMap* map) {
-  // 3-D view of the cache: x = head_dim (contiguous), y = token slot, z = (sequence, kv head)
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(L->D), static_cast<cuuint64_t>(L->max_tokens),
-                              static_cast<cuuint64_t>(L->max_batch) * L->Hk};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(L->D) * 2,
-                                 static_cast<cuuint64_t>(L->D) * 2 * L->max_tokens};
-  const cuuint32_t box[3] = {64, kTile, 1};
+  // 3-D view of the cache with 128-byte rows: x = 64 fp16 of a row half,
+  // y = (token slot, half), z = (sequence, kv head)
+  const cuuint64_t halves = static_cast<cuuint64_t>(L->D / 64);
+  const cuuint64_t dims[3] = {64, halves * L->max_tokens, static_cast<cuuint64_t>(L->max_batch) * L->Hk};
+  const cuuint64_t strides[2] = {128, 128 * halves * L->max_tokens};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kTile * halves), 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   return L->ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -628,7 +783,11 @@ cudaError_t decode_fast_configure(tla_layer* L) {
   cudaError_t e = L->D == 64 ? dispatch_configure<64>(L, &blocks) : dispatch_configure<128>(L, &blocks);
   if (e != cudaSuccess) return e;
   if (blocks <= 0) return cudaSuccess;
+#ifdef TLA_DECODE_CTAS_PER_SM
+  if (blocks > TLA_DECODE_CTAS_PER_SM) blocks = TLA_DECODE_CTAS_PER_SM;
+#endif
   L->decode_grid = blocks * L->ctx->sm_count;
+  if (L->decode_grid > 16 * L->D) L->decode_grid = 16 * L->D;  // merge slot table lives in the 16*D-float Q staging
   L->fast_decode = true;
   return cudaSuccess;
 }
@@ -655,6 +814,9 @@ cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_
   p.slot_offset = slot_offset;
   p.local_tokens = local_tokens;
   p.append = append;
+  // Few, long sequences split each (sequence, kv head) over many CTAs: merge
+  // those in a separate, fully parallel kernel instead of in the last CTA.
+  p.defer_merge = L->decode_grid > 4 * batch * L->Hk ? 1 : 0;
   return L->D == 64 ? dispatch_launch<64>(L, p, stream) : dispatch_launch<128>(L, p, stream);
 }
 
