@@ -414,6 +414,396 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   }
 }
 
+// ---------------------------------------------------------------- head_dim 64: two Q tiles per CTA
+// Two 128-row query tiles (Q0, Q1) of one (head, sequence) share every K/V
+// tile. Each tile has its own softmax warpgroup in which a thread owns one
+// whole row (no cross-warpgroup exchange), and the MMA warp alternates
+// between them: while warpgroup 0 turns S0(n) into P0(n), the tensor core
+// computes S1(n) and P1(n-1) V, and the other way round. P is written to
+// TMEM with tcgen05.st and read from there as the A operand of P V; O
+// accumulates in TMEM across tiles. A row's reference maximum only moves when
+// the tile maximum exceeds it by more than 2^8 (then O is rescaled in TMEM,
+// warp-uniformly, after the previous P V finished), so P stays <= 256 in fp16
+// and most tiles need no correction.
+constexpr int kThreads2 = 320;  // warps 0-3: softmax Q0, 4-7: softmax Q1, 8: TMA, 9: MMA
+constexpr float kRescaleLog2 = 8.f;
+
+struct P2Cfg {
+  static constexpr int kTile = 128 * 128;  // one [128][64] fp16 box
+  static constexpr int kST = 3;            // K/V stages
+  static constexpr int kQ0 = 0, kQ1 = kTile;
+  static constexpr int kK = 2 * kTile;
+  static constexpr int kV = kK + kST * kTile;
+  static constexpr int kBar = kV + kST * kTile;
+  // q_full, k_full/v_full/k_empty/v_empty [kST], s_full [2], p_full [2], o_done [2]
+  static constexpr int kNumBars = 1 + 4 * kST + 6;
+  static constexpr int kSmem = kBar + kNumBars * 8 + 16 + 1024;
+  // TMEM columns
+  static constexpr uint32_t kS = 0, kP = 256, kO = 384, kCols = 512;
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+
+
+// Two 32-column loads in flight before one wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[k * 32 + 0]), "=r"(r[k * 32 + 1]), "=r"(r[k * 32 + 2]), "=r"(r[k * 32 + 3]), "=r"(r[k * 32 + 4]),
+          "=r"(r[k * 32 + 5]), "=r"(r[k * 32 + 6]), "=r"(r[k * 32 + 7]), "=r"(r[k * 32 + 8]), "=r"(r[k * 32 + 9]),
+          "=r"(r[k * 32 + 10]), "=r"(r[k * 32 + 11]), "=r"(r[k * 32 + 12]), "=r"(r[k * 32 + 13]),
+          "=r"(r[k * 32 + 14]), "=r"(r[k * 32 + 15]), "=r"(r[k * 32 + 16]), "=r"(r[k * 32 + 17]),
+          "=r"(r[k * 32 + 18]), "=r"(r[k * 32 + 19]), "=r"(r[k * 32 + 20]), "=r"(r[k * 32 + 21]),
+          "=r"(r[k * 32 + 22]), "=r"(r[k * 32 + 23]), "=r"(r[k * 32 + 24]), "=r"(r[k * 32 + 25]),
+          "=r"(r[k * 32 + 26]), "=r"(r[k * 32 + 27]), "=r"(r[k * 32 + 28]), "=r"(r[k * 32 + 29]),
+          "=r"(r[k * 32 + 30]), "=r"(r[k * 32 + 31])
+        : "r"(taddr + k * 32));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// D (TMEM) += A (TMEM) * B (shared memory descriptor)
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// 2^x on the FMA pipe, for part of the softmax exponentials (the MUFU unit is the
+// bottleneck at head_dim 64). Cody-Waite split x = j + f with j = rint(x) (the
+// 1.5 * 2^23 rounding trick, j ends up in the low mantissa bits), f in [-0.5, 0.5];
+// 2^f from a cubic least-squares fit on Chebyshev nodes of [-0.5, 0.5]
+// (max relative error 7.7e-5, below fp16 resolution); 2^j is added to the
+// exponent field. Inputs below -126 (masked scores) give a subnormal that
+// rounds to 0 in fp16.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.05508868f, f, 0.24260405f), f, 0.69327623f), f, 0.99992895f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+#ifdef TLA_PREFILL_TRACE
+// Optional pipeline trace (builds with -DTLA_PREFILL_TRACE only): SM clock of
+// each event of block 0, [tile][event]; read with tla_debug_prefill_trace.
+__device__ unsigned long long g_prefill_trace[64][16];
+#define PTRACE(ev, n) \
+  do { \
+    if (blockIdx.x == 0 && (n) < 64) g_prefill_trace[(n)][(ev)] = clock64(); \
+  } while (0)
+#else
+#define PTRACE(ev, n) \
+  do { \
+  } while (0)
+#endif
+
+#ifndef TLA_PREFILL_POLY_EVERY
+#define TLA_PREFILL_POLY_EVERY 0  // every n-th pair of exponentials goes to the FMA pipe (0: none)
+#endif
+
+template <typename OUT>
+__global__ void __launch_bounds__(kThreads2, 1) prefill_tc2_kernel(const __grid_constant__ PrefillParams p) {
+  using C = P2Cfg;
+  constexpr int D = 64;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + C::kST;
+  uint64_t* k_empty = v_full + C::kST;
+  uint64_t* v_empty = k_empty + C::kST;
+  uint64_t* s_full = v_empty + C::kST;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const int bh_count = p.batch * p.Hq;
+  const int m = p.num_m - 1 - static_cast<int>(blockIdx.x) / bh_count;  // 256-row block, longest first
+  const int bh = static_cast<int>(blockIdx.x) % bh_count;
+  const int b = bh / p.Hq, h = bh - b * p.Hq, kvh = h / p.G;
+  const int start = p.start[b];
+  const int row0 = m * 256;
+  const int rows = min(256, p.S - row0);
+  const int pmin = start + row0, pmax = start + row0 + rows - 1;
+  const int first_min = p.sliding > 0 ? max(0, pmin - p.sliding + 1) : 0;
+  const int j0 = first_min / kCols, j1 = pmax / kCols;
+  const int N = j1 - j0 + 1;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < C::kST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    if (*abort_flag) return;
+    if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
+  };
+
+  if (warp == 8) {
+    // ================================================================ TMA producer
+    if (lane == 0) {
+      tma_prefetch(&p.tm_q);
+      tma_prefetch(&p.tm_k);
+      tma_prefetch(&p.tm_v);
+      mbar_arrive_expect_tx(q_full, 2 * C::kTile);
+      tma_load_3d(smem + C::kQ0, &p.tm_q, q_full, 0, row0, b * p.Hq + h);
+      tma_load_3d(smem + C::kQ1, &p.tm_q, q_full, 0, row0 + 128, b * p.Hq + h);
+      for (int n = 0; n < N; ++n) {
+        const int st = n % C::kST;
+        const uint32_t ph = ((n / C::kST) & 1) ^ 1;
+        const int y = (j0 + n) * kCols, z = b * p.Hk + kvh;
+        wait(&k_empty[st], ph);
+        if (!*abort_flag) {
+          mbar_arrive_expect_tx(&k_full[st], C::kTile);
+          tma_load_3d(smem + C::kK + st * C::kTile, &p.tm_k, &k_full[st], 0, y, z);
+        }
+        wait(&v_empty[st], ph);
+        if (!*abort_flag) {
+          mbar_arrive_expect_tx(&v_full[st], C::kTile);
+          tma_load_3d(smem + C::kV + st * C::kTile, &p.tm_v, &v_full[st], 0, y, z);
+        }
+      }
+      for (int n = max(0, N - C::kST); n < N; ++n) {  // no copies in flight at exit
+        wait(&k_full[n % C::kST], (n / C::kST) & 1);
+        wait(&v_full[n % C::kST], (n / C::kST) & 1);
+      }
+    }
+  } else if (warp == 9) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdS = idesc_f16(128, kCols, false);
+      constexpr uint32_t kIdO = idesc_f16(128, D, true);
+      const uint32_t q0 = smem_u32(smem + C::kQ0), q1 = smem_u32(smem + C::kQ1);
+      auto issue_s = [&](int t, int n) {  // S_t = Q_t K(n)^T
+        const uint32_t kb = smem_u32(smem + C::kK + (n % C::kST) * C::kTile);
+        const uint32_t qb = t == 0 ? q0 : q1;
+        if (!*abort_flag) {
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_f16(tmem + C::kS + t * 128, sdesc(qb + kk * 32, 16, 1024), sdesc(kb + kk * 32, 16, 1024), kIdS,
+                    kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int n) {  // O_t += P_t V(n)
+        const uint32_t vb = smem_u32(smem + C::kV + (n % C::kST) * C::kTile);
+        if (!*abort_flag) {
+#pragma unroll
+          for (int kk = 0; kk < kCols / 16; ++kk)
+            mma_f16_ts(tmem + C::kO + t * D, tmem + C::kP + t * 64 + kk * 8, sdesc(vb + kk * 2048, 16384, 1024),
+                       kIdO, (n > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&o_done[t]);
+      };
+      wait(q_full, 0);
+      wait(&k_full[0], 0);
+      tc_fence_after();
+      issue_s(0, 0);
+      issue_s(1, 0);
+      mma_commit(&k_empty[0]);
+      for (int n = 0; n < N; ++n) {
+        const bool more = n + 1 < N;
+        const int st1 = (n + 1) % C::kST;
+        wait(&p_full[0], n & 1);  // S0(n) consumed, P0(n) in TMEM
+        PTRACE(8, n);
+        if (more) wait(&k_full[st1], ((n + 1) / C::kST) & 1);
+        wait(&v_full[n % C::kST], (n / C::kST) & 1);
+        tc_fence_after();
+        PTRACE(9, n);
+        if (more) issue_s(0, n + 1);
+        issue_pv(0, n);
+        wait(&p_full[1], n & 1);
+        tc_fence_after();
+        PTRACE(10, n);
+        if (more) {
+          issue_s(1, n + 1);
+          mma_commit(&k_empty[st1]);
+        }
+        issue_pv(1, n);
+        mma_commit(&v_empty[n % C::kST]);
+        PTRACE(11, n);
+      }
+    }
+  } else {
+    // ================================================================ softmax (warpgroup t, row r)
+    const int t = warp >> 2;
+    const int r = tid & 127;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t s_addr = lane_addr + C::kS + t * 128;
+    const uint32_t p_addr = lane_addr + C::kP + t * 64;
+    const uint32_t o_addr = lane_addr + C::kO + t * D;
+    const int pr = start + row0 + t * 128 + r;
+    const int first_r = p.sliding > 0 ? max(0, pr - p.sliding + 1) : 0;
+    const float sl2 = p.scale_log2;
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int n = 0; n < N; ++n) {
+      const int tok0 = (j0 + n) * kCols;
+      const bool masked = tok0 + kCols - 1 > pr || tok0 < first_r;
+      wait(&s_full[t], n & 1);
+      __syncwarp();
+      tc_fence_after();
+      if ((warp & 3) == 0 && lane == 0) PTRACE(4 * t + 0, n);
+      // pass 1: row maximum (log2 units), 64 columns per step
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        float v[64];
+        tmem_ld64(s_addr + hf * 64, v);
+        if (!masked) {
+#pragma unroll
+          for (int i = 0; i < 64; i += 4) {
+            mx[0] = fmaxf(mx[0], v[i]);
+            mx[1] = fmaxf(mx[1], v[i + 1]);
+            mx[2] = fmaxf(mx[2], v[i + 2]);
+            mx[3] = fmaxf(mx[3], v[i + 3]);
+          }
+        } else {
+          const int lo = first_r - (tok0 + hf * 64), hi = pr - (tok0 + hf * 64);  // valid columns [lo, hi]
+#pragma unroll
+          for (int i = 0; i < 64; ++i) mx[i & 3] = fmaxf(mx[i & 3], (i >= lo && i <= hi) ? v[i] : -INFINITY);
+        }
+      }
+      if ((warp & 3) == 0 && lane == 0) PTRACE(4 * t + 2, n);
+      const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+      // move the reference maximum only when this tile exceeds it by more than 2^8
+      const bool grow = m_tile > m_run + kRescaleLog2;
+      if (n > 0) {  // P_t is free and O_t stable once the previous P V finished
+        wait(&o_done[t], (n - 1) & 1);
+        __syncwarp();
+        tc_fence_after();
+      }
+      if ((warp & 3) == 0 && lane == 0) PTRACE(4 * t + 1, n);
+      if (__any_sync(0xffffffffu, grow)) {
+        const float m_new = grow ? m_tile : m_run;
+        // 0 while the row has seen no unmasked token (O and l are still zero), 1 when unchanged
+        const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - m_new);
+        if (n > 0) {  // rescale O in TMEM
+          float o[32];
+          uint32_t u[32];
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            tmem_ld32(o_addr + c * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * alpha);
+            tmem_st32(o_addr + c * 32, u);
+          }
+        }
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      const float mu = m_run == -INFINITY ? 0.f : m_run;
+      // pass 2: P = 2^(s*scale - mu) to TMEM as fp16 pairs
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        float v[64];
+        tmem_ld64(s_addr + hf * 64, v);
+        uint32_t pk[32];
+        if (!masked) {
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const bool poly = TLA_PREFILL_POLY_EVERY > 0 && (i / 2) % TLA_PREFILL_POLY_EVERY == TLA_PREFILL_POLY_EVERY - 1;
+            const float x0 = fmaf(v[i], sl2, -mu), x1 = fmaf(v[i + 1], sl2, -mu);
+            const float e0 = poly ? ex2_poly(x0) : ex2(x0);
+            const float e1 = poly ? ex2_poly(x1) : ex2(x1);
+            sum[(i >> 1) & 3] += e0 + e1;
+            pk[i / 2] = pack_half2(e0, e1);
+          }
+        } else {
+          const int lo = first_r - (tok0 + hf * 64), hi = pr - (tok0 + hf * 64);
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const float e0 = (i >= lo && i <= hi) ? ex2(fmaf(v[i], sl2, -mu)) : 0.f;
+            const float e1 = (i + 1 >= lo && i + 1 <= hi) ? ex2(fmaf(v[i + 1], sl2, -mu)) : 0.f;
+            sum[(i >> 1) & 3] += e0 + e1;
+            pk[i / 2] = pack_half2(e0, e1);
+          }
+        }
+        tmem_st32(p_addr + hf * 32, pk);
+      }
+      tmem_wait_st();
+      l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+      if ((warp & 3) == 0 && lane == 0) PTRACE(4 * t + 3, n);
+    }
+    // ---- epilogue
+    wait(&o_done[t], (N - 1) & 1);
+    __syncwarp();
+    tc_fence_after();
+    const int row = row0 + t * 128 + r;
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      float o[32];
+      tmem_ld32(o_addr + c * 32, o);
+      if (row < p.S) {
+        OUT* dst = static_cast<OUT*>(p.out) + ((static_cast<size_t>(b) * p.S + row) * p.Hq + h) * D + c * 32;
+        if constexpr (sizeof(OUT) == 2) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8)
+            *reinterpret_cast<uint4*>(dst + i) =
+                make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv), pack_half2(o[i + 2] * inv, o[i + 3] * inv),
+                           pack_half2(o[i + 4] * inv, o[i + 5] * inv), pack_half2(o[i + 6] * inv, o[i + 7] * inv));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dst + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kCols) : "memory");
+  }
+}
+
 CUresult make_map(const tla_layer* L, void* base, uint64_t rows, uint64_t planes, CUtensorMap* map) {
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(L->D), rows, planes};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(L->D) * 2, static_cast<cuuint64_t>(L->D) * 2 * rows};
@@ -432,6 +822,12 @@ cudaError_t set_smem() {
 
 }  // namespace
 
+#ifdef TLA_PREFILL_TRACE
+extern "C" int tla_debug_prefill_trace(unsigned long long* host, int count) {
+  return cudaMemcpyFromSymbol(host, g_prefill_trace, sizeof(unsigned long long) * count) == cudaSuccess ? 0 : -1;
+}
+#endif
+
 cudaError_t prefill_fast_configure(tla_layer* L) {
   L->fast_prefill = false;
   if (L->cache_fp32 || (L->D != 64 && L->D != 128) || L->G <= 0 || L->ctx->encode_tiled == nullptr) return cudaSuccess;
@@ -441,8 +837,11 @@ cudaError_t prefill_fast_configure(tla_layer* L) {
     return cudaSuccess;
   cudaError_t e;
   if (L->D == 64) {
-    e = L->io_fp32 ? set_smem<64, float>() : set_smem<64, __half>();
-    L->prefill_smem = PCfg<64>::kSmem;
+    e = L->io_fp32 ? cudaFuncSetAttribute(prefill_tc2_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          P2Cfg::kSmem)
+                   : cudaFuncSetAttribute(prefill_tc2_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          P2Cfg::kSmem);
+    L->prefill_smem = P2Cfg::kSmem;
   } else {
     e = L->io_fp32 ? set_smem<128, float>() : set_smem<128, __half>();
     L->prefill_smem = PCfg<128>::kSmem;
@@ -471,15 +870,17 @@ cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32
   p.G = L->G;
   p.sliding = L->sliding;
   p.batch = batch;
-  p.num_m = (seq_len + kRows - 1) / kRows;
   p.scale_log2 = L->attn_scale * kLog2e;
-  const dim3 grid(static_cast<unsigned>(p.num_m * batch * L->Hq));
   if (L->D == 64) {
+    p.num_m = (seq_len + 255) / 256;
+    const dim3 grid(static_cast<unsigned>(p.num_m * batch * L->Hq));
     if (L->io_fp32)
-      prefill_tc_kernel<64, float><<<grid, kThreads, PCfg<64>::kSmem, stream>>>(p);
+      prefill_tc2_kernel<float><<<grid, kThreads2, P2Cfg::kSmem, stream>>>(p);
     else
-      prefill_tc_kernel<64, __half><<<grid, kThreads, PCfg<64>::kSmem, stream>>>(p);
+      prefill_tc2_kernel<__half><<<grid, kThreads2, P2Cfg::kSmem, stream>>>(p);
   } else {
+    p.num_m = (seq_len + kRows - 1) / kRows;
+    const dim3 grid(static_cast<unsigned>(p.num_m * batch * L->Hq));
     if (L->io_fp32)
       prefill_tc_kernel<128, float><<<grid, kThreads, PCfg<128>::kSmem, stream>>>(p);
     else

@@ -2,6 +2,7 @@
 // surface, packages/three-llm/src/tsl/TSLAttention.ts:19-448), argument
 // validation and kernel dispatch.
 #include <math.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -54,6 +55,7 @@ struct DeviceGuard {
 
 int from_cuda(cudaError_t e) {
   if (e == cudaSuccess) return TLA_OK;
+  if (getenv("TLA_DEBUG")) fprintf(stderr, "tla: CUDA error %d: %s\n", static_cast<int>(e), cudaGetErrorString(e));
   if (e == cudaErrorMemoryAllocation) return TLA_ERR_OUT_OF_MEMORY;
   return TLA_ERR_CUDA;
 }
