@@ -239,6 +239,33 @@ cudaError_t attend_t(const tla_layer* L, const float* qscr, const int32_t* start
 
 }  // namespace
 
+// EPL consecutive elements as floats, with a single vector load.
+template <typename IO, int EPL>
+__device__ __forceinline__ void load_vec(const IO* p, float (&x)[EPL]) {
+  if constexpr (sizeof(IO) == 2 && EPL == 2) {
+    const __half2 h = *reinterpret_cast<const __half2*>(p);
+    x[0] = __low2float(h);
+    x[1] = __high2float(h);
+  } else if constexpr (sizeof(IO) == 2 && EPL == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __half2 a = *reinterpret_cast<const __half2*>(&u.x), b = *reinterpret_cast<const __half2*>(&u.y);
+    x[0] = __low2float(a);
+    x[1] = __high2float(a);
+    x[2] = __low2float(b);
+    x[3] = __high2float(b);
+  } else if constexpr (EPL == 2) {
+    const float2 f = *reinterpret_cast<const float2*>(p);
+    x[0] = f.x;
+    x[1] = f.y;
+  } else {
+    const float4 f = *reinterpret_cast<const float4*>(p);
+    x[0] = f.x;
+    x[1] = f.y;
+    x[2] = f.z;
+    x[3] = f.w;
+  }
+}
+
 // Warp-per-token variant for head_dim 64 / 128 and an fp16 cache: lane l holds
 // elements [l*EPL, (l+1)*EPL) of every head of the token, head norms are warp
 // reductions and the rotate-half partner comes from lane +/- half/EPL.
@@ -262,63 +289,76 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(LayerArgs a, cons
   const bool lo_side = d0 < half;
   const bool rot = half > 0 && d0 < a.rotary;
   const int src = !rot ? lane : (lo_side ? lane + half / EPL : lane - half / EPL);
-  float c[EPL], sn[EPL];
+  float c_[EPL], sn[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
-    c[e] = 1.f;
+    c_[e] = 1.f;
     sn[e] = 0.f;
     const int j = lo_side ? d0 + e : d0 + e - half;
-    if (rot && j < a.pair_count) rope_cos_sin(pos, a.inv_freq[j], &c[e], &sn[e]);
+    if (rot && j < a.pair_count) rope_cos_sin(pos, a.inv_freq[j], &c_[e], &sn[e]);
   }
   const int heads = Hq + 2 * Hk;
   const IO* row = qkv + static_cast<size_t>(ti) * heads * D;
   __half* kc = static_cast<__half*>(a.k_cache);
   __half* vc = static_cast<__half*>(a.v_cache);
-  for (int hh = 0; hh < heads; ++hh) {
-    float x[EPL];
+  constexpr int kChunk = 8;  // heads whose loads are in flight together
+  for (int h0 = 0; h0 < heads; h0 += kChunk) {
+    float xs[kChunk][EPL];
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) x[e] = to_f32(row[hh * D + d0 + e]);
-    const float* w = hh < Hq ? a.q_norm : (hh < Hq + Hk ? a.k_norm : nullptr);
-    const bool norm = hh < Hq + Hk ? w != nullptr : a.v_norm != 0;
-    if (norm) {  // math.ts:78-97
-      float ss = 0.f;
+    for (int c = 0; c < kChunk; ++c) {
+      if (h0 + c < heads)
+        load_vec<IO, EPL>(row + (h0 + c) * D + d0, xs[c]);  // one 4-16 byte load per lane and head
+      else
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) ss += x[e] * x[e];
-      ss = warp_sum(ss);
-      const float inv_rms = 1.f / sqrtf(ss / static_cast<float>(D) + a.rms_eps);
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        const float sc = w == nullptr ? 1.f : (a.offset_rms ? 1.f + w[d0 + e] : w[d0 + e]);
-        x[e] = x[e] * inv_rms * sc;
-      }
+        for (int e = 0; e < EPL; ++e) xs[c][e] = 0.f;
     }
-    if (hh < Hq + Hk) {  // RoPE, math.ts:134-147
-      float y[EPL];
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        const float partner = __shfl_sync(0xffffffffu, x[e], src);
-        y[e] = x[e];
-        const int j = lo_side ? d0 + e : d0 + e - half;
-        if (rot && j < a.pair_count) y[e] = (x[e] * c[e] + (lo_side ? -partner : partner) * sn[e]) * a.attn_factor;
+    for (int c = 0; c < kChunk; ++c) {
+      const int hh = h0 + c;
+      if (hh >= heads) break;
+      float* x = xs[c];
+      const float* w = hh < Hq ? a.q_norm : (hh < Hq + Hk ? a.k_norm : nullptr);
+      const bool norm = hh < Hq + Hk ? w != nullptr : a.v_norm != 0;
+      if (norm) {  // math.ts:78-97
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) ss += x[e] * x[e];
+        ss = warp_sum(ss);
+        const float inv_rms = 1.f / sqrtf(ss / static_cast<float>(D) + a.rms_eps);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          const float sc = w == nullptr ? 1.f : (a.offset_rms ? 1.f + w[d0 + e] : w[d0 + e]);
+          x[e] = x[e] * inv_rms * sc;
+        }
       }
+      if (hh < Hq + Hk) {  // RoPE, math.ts:134-147
+        float y[EPL];
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) x[e] = y[e];
+        for (int e = 0; e < EPL; ++e) {
+          const float partner = __shfl_sync(0xffffffffu, x[e], src);
+          y[e] = x[e];
+          const int j = lo_side ? d0 + e : d0 + e - half;
+          if (rot && j < a.pair_count) y[e] = (x[e] * c_[e] + (lo_side ? -partner : partner) * sn[e]) * a.attn_factor;
+        }
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) x[e] = y[e];
+      }
+      __half hv[EPL];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) hv[e] = __float2half_rn(x[e]);
+      __half* dst;
+      if (hh < Hq)
+        dst = qscr + ((static_cast<size_t>(b) * Hq + hh) * seq_len + t) * D + d0;
+      else if (hh < Hq + Hk)
+        dst = kc + ((static_cast<size_t>(b) * Hk + (hh - Hq)) * a.max_tokens + pos) * D + d0;
+      else
+        dst = vc + ((static_cast<size_t>(b) * Hk + (hh - Hq - Hk)) * a.max_tokens + pos) * D + d0;
+      if constexpr (EPL == 2)
+        *reinterpret_cast<__half2*>(dst) = __halves2half2(hv[0], hv[1]);
+      else
+        *reinterpret_cast<uint2*>(dst) = make_uint2(*reinterpret_cast<uint32_t*>(&hv[0]),
+                                                    *reinterpret_cast<uint32_t*>(&hv[2]));
     }
-    __half hv[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) hv[e] = __float2half_rn(x[e]);
-    __half* dst;
-    if (hh < Hq)
-      dst = qscr + ((static_cast<size_t>(b) * Hq + hh) * seq_len + t) * D + d0;
-    else if (hh < Hq + Hk)
-      dst = kc + ((static_cast<size_t>(b) * Hk + (hh - Hq)) * a.max_tokens + pos) * D + d0;
-    else
-      dst = vc + ((static_cast<size_t>(b) * Hk + (hh - Hq - Hk)) * a.max_tokens + pos) * D + d0;
-    if constexpr (EPL == 2)
-      *reinterpret_cast<__half2*>(dst) = __halves2half2(hv[0], hv[1]);
-    else
-      *reinterpret_cast<uint2*>(dst) = make_uint2(*reinterpret_cast<uint32_t*>(&hv[0]),
-                                                  *reinterpret_cast<uint32_t*>(&hv[2]));
   }
 }
 
