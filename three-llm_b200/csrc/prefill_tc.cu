@@ -425,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 // the tile maximum exceeds it by more than 2^8 (then O is rescaled in TMEM,
 // warp-uniformly, after the previous P V finished), so P stays <= 256 in fp16
 // and most tiles need no correction.
-constexpr int kThreads2 = 320;  // warps 0-3: softmax Q0, 4-7: softmax Q1, 8: TMA, 9: MMA
+constexpr int kThreads2 = 576;  // warps 0-15: four softmax warpgroups, 16: TMA, 17: MMA
 constexpr float kRescaleLog2 = 8.f;
 
 struct P2Cfg {
@@ -437,7 +437,8 @@ struct P2Cfg {
   static constexpr int kBar = kV + kST * kTile;
   // q_full, k_full/v_full/k_empty/v_empty [kST], s_full [2], p_full [2], o_done [2]
   static constexpr int kNumBars = 1 + 4 * kST + 6;
-  static constexpr int kSmem = kBar + kNumBars * 8 + 16 + 1024;
+  static constexpr int kXch = kBar + kNumBars * 8 + 16;  // [2][2 tiles][2 halves][128] row maxima / sums
+  static constexpr int kSmem = kXch + 2 * 2 * 2 * 128 * 4 + 1024;
   // TMEM columns
   static constexpr uint32_t kS = 0, kP = 256, kO = 384, kCols = 512;
 };
@@ -453,6 +454,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
 
 
 
@@ -561,13 +570,13 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill_tc2_kernel(const __grid_
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 256);
       mbar_init(&o_done[i], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == 17) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(C::kCols)
                  : "memory");
@@ -582,7 +591,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill_tc2_kernel(const __grid_
     if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
   };
 
-  if (warp == 8) {
+  if (warp == 16) {
     // ================================================================ TMA producer
     if (lane == 0) {
       tma_prefetch(&p.tm_q);
@@ -611,7 +620,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill_tc2_kernel(const __grid_
         wait(&v_full[n % C::kST], (n / C::kST) & 1);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 17) {
     // ================================================================ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdS = idesc_f16(128, kCols, false);
@@ -668,46 +677,58 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill_tc2_kernel(const __grid_
       }
     }
   } else {
-    // ================================================================ softmax (warpgroup t, row r)
-    const int t = warp >> 2;
+    // ================================================================ softmax
+    // warpgroup g: Q tile t = g >> 1, column half hc = g & 1. The two warpgroups
+    // of a tile hold the same rows (TMEM lanes); they meet once per tile in
+    // shared memory for the row maximum and keep separate row sums.
+    const int g = warp >> 2, t = g >> 1, hc = g & 1;
     const int r = tid & 127;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t s_addr = lane_addr + C::kS + t * 128;
-    const uint32_t p_addr = lane_addr + C::kP + t * 64;
-    const uint32_t o_addr = lane_addr + C::kO + t * D;
+    const uint32_t s_addr = lane_addr + C::kS + t * 128 + hc * 64;  // this half's 64 S columns
+    const uint32_t p_addr = lane_addr + C::kP + t * 64 + hc * 32;   // its 32 columns of fp16 pairs
+    const uint32_t o_addr = lane_addr + C::kO + t * D + hc * 32;    // its 32 output columns
+    float* xch = reinterpret_cast<float*>(smem + C::kXch);
+    auto xslot = [&](int buf, int half) -> float& { return xch[((buf * 2 + t) * 2 + half) * 128 + r]; };
+    const bool tracer = hc == 0 && (warp & 3) == 0 && lane == 0;
     const int pr = start + row0 + t * 128 + r;
     const int first_r = p.sliding > 0 ? max(0, pr - p.sliding + 1) : 0;
     const float sl2 = p.scale_log2;
-    float m_run = -INFINITY, l_run = 0.f;
+    float m_run = -INFINITY, l_part = 0.f;
     for (int n = 0; n < N; ++n) {
-      const int tok0 = (j0 + n) * kCols;
-      const bool masked = tok0 + kCols - 1 > pr || tok0 < first_r;
+      const int tok0 = (j0 + n) * kCols + hc * 64;  // first token of this half
+      const bool masked = tok0 + 63 > pr || tok0 < first_r;
+      const int lo = first_r - tok0, hi = pr - tok0;  // valid columns [lo, hi] of this half
       wait(&s_full[t], n & 1);
       __syncwarp();
       tc_fence_after();
-      if ((warp & 3) == 0 && lane == 0) PTRACE(4 * t + 0, n);
-      // pass 1: row maximum (log2 units), 64 columns per step
+      if (tracer) PTRACE(4 * t + 0, n);
+      // pass 1: this half's maximum, then the row maximum with the other half
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
-      for (int hf = 0; hf < 2; ++hf) {
-        float v[64];
-        tmem_ld64(s_addr + hf * 64, v);
+      for (int ch = 0; ch < 2; ++ch) {
+        float v[32];
+        tmem_ld32(s_addr + ch * 32, v);
         if (!masked) {
 #pragma unroll
-          for (int i = 0; i < 64; i += 4) {
+          for (int i = 0; i < 32; i += 4) {
             mx[0] = fmaxf(mx[0], v[i]);
             mx[1] = fmaxf(mx[1], v[i + 1]);
             mx[2] = fmaxf(mx[2], v[i + 2]);
             mx[3] = fmaxf(mx[3], v[i + 3]);
           }
         } else {
-          const int lo = first_r - (tok0 + hf * 64), hi = pr - (tok0 + hf * 64);  // valid columns [lo, hi]
 #pragma unroll
-          for (int i = 0; i < 64; ++i) mx[i & 3] = fmaxf(mx[i & 3], (i >= lo && i <= hi) ? v[i] : -INFINITY);
+          for (int i = 0; i < 32; ++i) {
+            const int k = ch * 32 + i;
+            mx[i & 3] = fmaxf(mx[i & 3], (k >= lo && k <= hi) ? v[i] : -INFINITY);
+          }
         }
       }
-      if ((warp & 3) == 0 && lane == 0) PTRACE(4 * t + 2, n);
-      const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+      const float pm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      xslot(n & 1, hc) = pm;
+      named_barrier_sync(1 + t, 256);
+      const float m_tile = fmaxf(pm, xslot(n & 1, hc ^ 1)) * sl2;
+      if (tracer) PTRACE(4 * t + 2, n);
       // move the reference maximum only when this tile exceeds it by more than 2^8
       const bool grow = m_tile > m_run + kRescaleLog2;
       if (n > 0) {  // P_t is free and O_t stable once the previous P V finished
@@ -715,36 +736,33 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill_tc2_kernel(const __grid_
         __syncwarp();
         tc_fence_after();
       }
-      if ((warp & 3) == 0 && lane == 0) PTRACE(4 * t + 1, n);
+      if (tracer) PTRACE(4 * t + 1, n);
       if (__any_sync(0xffffffffu, grow)) {
         const float m_new = grow ? m_tile : m_run;
         // 0 while the row has seen no unmasked token (O and l are still zero), 1 when unchanged
         const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - m_new);
-        if (n > 0) {  // rescale O in TMEM
+        if (n > 0) {  // rescale this half of O in TMEM
           float o[32];
           uint32_t u[32];
+          tmem_ld32(o_addr, o);
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            tmem_ld32(o_addr + c * 32, o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * alpha);
-            tmem_st32(o_addr + c * 32, u);
-          }
+          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * alpha);
+          tmem_st32(o_addr, u);
         }
-        l_run *= alpha;
+        l_part *= alpha;
         m_run = m_new;
       }
       const float mu = m_run == -INFINITY ? 0.f : m_run;
       // pass 2: P = 2^(s*scale - mu) to TMEM as fp16 pairs
       float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-      for (int hf = 0; hf < 2; ++hf) {
-        float v[64];
-        tmem_ld64(s_addr + hf * 64, v);
-        uint32_t pk[32];
+      for (int ch = 0; ch < 2; ++ch) {
+        float v[32];
+        tmem_ld32(s_addr + ch * 32, v);
+        uint32_t pk[16];
         if (!masked) {
 #pragma unroll
-          for (int i = 0; i < 64; i += 2) {
+          for (int i = 0; i < 32; i += 2) {
             const bool poly = TLA_PREFILL_POLY_EVERY > 0 && (i / 2) % TLA_PREFILL_POLY_EVERY == TLA_PREFILL_POLY_EVERY - 1;
             const float x0 = fmaf(v[i], sl2, -mu), x1 = fmaf(v[i + 1], sl2, -mu);
             const float e0 = poly ? ex2_poly(x0) : ex2(x0);
@@ -753,52 +771,52 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill_tc2_kernel(const __grid_
             pk[i / 2] = pack_half2(e0, e1);
           }
         } else {
-          const int lo = first_r - (tok0 + hf * 64), hi = pr - (tok0 + hf * 64);
 #pragma unroll
-          for (int i = 0; i < 64; i += 2) {
-            const float e0 = (i >= lo && i <= hi) ? ex2(fmaf(v[i], sl2, -mu)) : 0.f;
-            const float e1 = (i + 1 >= lo && i + 1 <= hi) ? ex2(fmaf(v[i + 1], sl2, -mu)) : 0.f;
+          for (int i = 0; i < 32; i += 2) {
+            const int k = ch * 32 + i;
+            const float e0 = (k >= lo && k <= hi) ? ex2(fmaf(v[i], sl2, -mu)) : 0.f;
+            const float e1 = (k + 1 >= lo && k + 1 <= hi) ? ex2(fmaf(v[i + 1], sl2, -mu)) : 0.f;
             sum[(i >> 1) & 3] += e0 + e1;
             pk[i / 2] = pack_half2(e0, e1);
           }
         }
-        tmem_st32(p_addr + hf * 32, pk);
+        tmem_st16(p_addr + ch * 16, pk);
       }
       tmem_wait_st();
-      l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+      l_part += (sum[0] + sum[1]) + (sum[2] + sum[3]);
       tc_fence_before();
       mbar_arrive(&p_full[t]);
-      if ((warp & 3) == 0 && lane == 0) PTRACE(4 * t + 3, n);
+      if (tracer) PTRACE(4 * t + 3, n);
     }
-    // ---- epilogue
+    // ---- epilogue: row sum of both halves, normalise and store this half's 32 columns
+    xslot(N & 1, hc) = l_part;
+    named_barrier_sync(1 + t, 256);
+    const float l_run = l_part + xslot(N & 1, hc ^ 1);
     wait(&o_done[t], (N - 1) & 1);
     __syncwarp();
     tc_fence_after();
     const int row = row0 + t * 128 + r;
     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    float o[32];
+    tmem_ld32(o_addr, o);
+    if (row < p.S) {
+      OUT* dst = static_cast<OUT*>(p.out) + ((static_cast<size_t>(b) * p.S + row) * p.Hq + h) * D + hc * 32;
+      if constexpr (sizeof(OUT) == 2) {
 #pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      float o[32];
-      tmem_ld32(o_addr + c * 32, o);
-      if (row < p.S) {
-        OUT* dst = static_cast<OUT*>(p.out) + ((static_cast<size_t>(b) * p.S + row) * p.Hq + h) * D + c * 32;
-        if constexpr (sizeof(OUT) == 2) {
+        for (int i = 0; i < 32; i += 8)
+          *reinterpret_cast<uint4*>(dst + i) =
+              make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv), pack_half2(o[i + 2] * inv, o[i + 3] * inv),
+                         pack_half2(o[i + 4] * inv, o[i + 5] * inv), pack_half2(o[i + 6] * inv, o[i + 7] * inv));
+      } else {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8)
-            *reinterpret_cast<uint4*>(dst + i) =
-                make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv), pack_half2(o[i + 2] * inv, o[i + 3] * inv),
-                           pack_half2(o[i + 4] * inv, o[i + 5] * inv), pack_half2(o[i + 6] * inv, o[i + 7] * inv));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(dst + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
-        }
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(dst + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 17) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kCols) : "memory");
   }
