@@ -246,8 +246,13 @@ class LongCtx:
         gen = torch.Generator(device=device)
         gen.manual_seed(5 + rank)
         self.shards = []
+        self.exchange = None
+        mode = getattr(args, "exchange", "p2p")
+        if world > 1 and mode == "p2p":  # one peer exchange serves all layers
+            self.exchange = sharding.PeerExchange(rank, world, Hq * (D + 2) * 4, device)
         for _ in range(L):
-            s = sharding.SequenceShardedDecode(Hq, Hk, D, T, rank, world, {"ropeTheta": w["theta"]})
+            s = sharding.SequenceShardedDecode(Hq, Hk, D, T, rank, world, {"ropeTheta": w["theta"]},
+                                               exchange=mode, peer_exchange=self.exchange)
             fill_cache_random(s.layer, gen, torch)
             self.shards.append(s)
         self.layers = [s.layer for s in self.shards]
@@ -260,14 +265,22 @@ class LongCtx:
         self.bytes_per_launch = decode_seq_bytes(local, Hq, Hk, D)
         self.tokens_per_step = 1 / world
         self.launches_per_step = 2 * L
-        self.kernel = "decode_fast_kernel<128,half> partial + NCCL all-gather + combine_lse_kernel"
+        if world == 1:
+            self.kernel = "decode_fast_kernel<128,half> partial + combine_lse_kernel"
+            xname = "none"
+        elif mode == "p2p":
+            self.kernel = "decode_fast_kernel<128,half> partial + exchange_combine_kernel (NVLink stores + merge)"
+            xname = "peer-memory exchange kernel (NVLink stores, flag wait) + LSE merge"
+        else:
+            self.kernel = "decode_fast_kernel<128,half> partial + NCCL all-gather + combine_lse_kernel"
+            xname = "NCCL all-gather of (m,l,o) + LSE merge"
         self.config = {"workload": "long_ctx (config 5): 32 layers x 32q/8kv heads x d128, one sequence, 131072 "
                                    "cached tokens + 1 new, fp16 KV, theta 5e5", "global_batch": 1,
-                       "parallelism": f"sequence blocks x{world}, NCCL all-gather of (m,l,o) + LSE merge per layer",
+                       "parallelism": f"sequence blocks x{world}, {xname} per layer",
                        "l2": "inputs larger than L2; no flush"}
         self.scaling = "strong"
         self.use_graph = True
-        self.config["launch"] = "32-layer step captured as one CUDA graph (partial kernel, all-gather, merge)"
+        self.config["launch"] = "32-layer step captured as one CUDA graph (partial kernel, exchange, merge)"
         self.outs = torch.empty(L, 1, Hq * D, dtype=torch.float16, device=device)
 
     def step(self, record=None):
@@ -293,8 +306,10 @@ class LongCtx:
         self.out_host.copy_(self.outs, non_blocking=True)
 
     def close(self):
-        for layer in self.layers:
-            layer.close()
+        for s in self.shards:
+            s.close()
+        if self.exchange is not None:
+            self.exchange.close()
 
 
 def run_prefill(pkg, torch, device, args):
@@ -475,6 +490,8 @@ def main():
     ap.add_argument("--ref-batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="long_ctx merge of the sequence shards across GPUs")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))

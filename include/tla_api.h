@@ -167,6 +167,32 @@ int tla_decode_partial(tla_layer* layer, const void* qkv, const int32_t* positio
 int tla_combine_lse(const float* partials, int32_t ranks, int32_t batch, int32_t head_count, int32_t head_dim,
                     const void* gate, void* out, uint32_t io_flags, void* stream);
 
+/* Peer-memory exchange for sequence-sharded decode across the GPUs of one
+ * node (no counterpart in the reference, which runs on one device). Each
+ * rank creates its exchange buffer (returning a 64-byte IPC handle), the
+ * ranks swap handles out of band, connect, and then per layer
+ * tla_exchange_combine pushes this rank's partial triples
+ * ([batch][head_count][head_dim + 2], as from tla_decode_partial) into every
+ * peer's buffer over NVLink, waits (bounded; TLA_ERR_TIMEOUT via
+ * tla_get_error) for all peers' triples of the same step and writes the
+ * log-sum-exp merge to out ([batch][head_count][head_dim], fp16 or with
+ * TLA_FLAG_IO_FP32 float32). Every rank must call it the same number of
+ * times; the step counter lives on the device, so the call can be captured
+ * in a CUDA graph. batch * head_count <= 1024. */
+typedef struct tla_exchange tla_exchange;
+int tla_exchange_create(tla_ctx* ctx, int32_t rank, int32_t ranks, size_t slot_bytes, tla_exchange** out,
+                        void* ipc_handle_out);
+int tla_exchange_connect(tla_exchange* exchange, const void* ipc_handles /* [ranks][64] */);
+int tla_exchange_combine(tla_exchange* exchange, const float* partial, int32_t batch, int32_t head_count,
+                         int32_t head_dim, const void* gate, void* out, uint32_t io_flags, void* stream);
+/* Same-process alternative to the IPC handles: tla_exchange_buffer returns
+ * this rank's buffer, tla_exchange_connect_buffers takes every rank's buffer
+ * as a device pointer this device can address (ranks on one device, or
+ * buffers the caller mapped itself). */
+int tla_exchange_buffer(tla_exchange* exchange, void** buffer_out);
+int tla_exchange_connect_buffers(tla_exchange* exchange, void* const* buffers /* [ranks] */);
+int tla_exchange_destroy(tla_exchange* exchange);
+
 /* reset() (TSLAttention.ts:434-441): zero the cache. A borrowing layer is a no-op. */
 int tla_cache_reset(tla_layer* layer, void* stream);
 

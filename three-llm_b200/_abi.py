@@ -30,7 +30,8 @@ EXPORTS = [
     "tla_status_string", "tla_create", "tla_destroy", "tla_get_error", "tla_rope_parameters", "tla_layer_create",
     "tla_layer_share_cache", "tla_layer_destroy", "tla_layer_cache_view", "tla_decode", "tla_prefill",
     "tla_decode_partial", "tla_combine_lse", "tla_cache_reset", "tla_cache_read", "tla_cache_write",
-    "tla_decode_noalloc",
+    "tla_decode_noalloc", "tla_exchange_create", "tla_exchange_connect", "tla_exchange_combine",
+    "tla_exchange_buffer", "tla_exchange_connect_buffers", "tla_exchange_destroy",
 ]
 
 
@@ -115,6 +116,12 @@ def lib():
         L.tla_cache_reset.argtypes = [P, P]
         L.tla_cache_read.argtypes = [P, i32, i32, i32, P, P]
         L.tla_cache_write.argtypes = [P, i32, i32, i32, P, P]
+        L.tla_exchange_create.argtypes = [P, i32, i32, ctypes.c_size_t, ctypes.POINTER(P), P]
+        L.tla_exchange_connect.argtypes = [P, P]
+        L.tla_exchange_combine.argtypes = [P, P, i32, i32, i32, P, P, u32, P]
+        L.tla_exchange_buffer.argtypes = [P, ctypes.POINTER(P)]
+        L.tla_exchange_connect_buffers.argtypes = [P, P]
+        L.tla_exchange_destroy.argtypes = [P]
         L.tla_decode_noalloc.argtypes = [ctypes.POINTER(AttnConfig), P, P, P, P, P, P, P, P, P, i32, P]
         for name in EXPORTS:
             if name != "tla_status_string":

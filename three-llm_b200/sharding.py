@@ -10,13 +10,21 @@ an exchange, plus the one place that needs one:
   tensor-parallel output projection. No collective.
 - sequence_shard: rank r owns the contiguous token block
   [r*T/N, (r+1)*T/N); every rank emits (m, l, o) per query head with
-  tla_decode_partial and one all-gather of those triples feeds tla_combine_lse.
+  tla_decode_partial, and the triples meet either through one all-gather of
+  the process group followed by tla_combine_lse ("nccl"), or through
+  PeerExchange ("p2p"): one kernel that stores them into every peer's buffer
+  over NVLink, waits for the peers' triples and merges them.
 """
+import ctypes
 from dataclasses import dataclass
 
 import torch
 
-from .attention import CUDAAttention, combine_lse
+from . import _abi
+from ._abi import check, lib
+from .attention import Context, CUDAAttention, _ptr, _stream, combine_lse
+
+IPC_HANDLE_BYTES = 64
 
 
 @dataclass(frozen=True)
@@ -61,17 +69,74 @@ def sequence_shard(total_tokens, world, rank):
     return SequenceShard(begin, end - begin, rank == world - 1)
 
 
+class PeerExchange:
+    """tla_exchange_*: gather + log-sum-exp merge of sequence-shard triples over peer memory.
+
+    Every rank of `group` constructs one with the same `slot_bytes` (the
+    byte size of one rank's [B, Hq, D+2] float32 triples); the IPC handles of
+    the ranks' buffers travel once through the process group. combine() is one
+    kernel launch per call, stream-ordered and graph-capturable; a peer that
+    never arrives ends the wait after about two seconds with TLA_ERR_TIMEOUT
+    on the context's error word.
+    """
+
+    def __init__(self, rank, world, slot_bytes, device=None, group=None, context=None):
+        if device is None:
+            device = torch.cuda.current_device()
+        elif isinstance(device, torch.device):
+            device = device.index or 0
+        self.context = context or Context.default(device)
+        self.rank, self.world = rank, world
+        h = ctypes.c_void_p()
+        handle = (ctypes.c_char * IPC_HANDLE_BYTES)()
+        check(lib().tla_exchange_create(self.context.handle, rank, world, slot_bytes, ctypes.byref(h), handle),
+              "tla_exchange_create")
+        self.handle = h
+        if group is not False and world > 1:
+            handles = [None] * world
+            torch.distributed.all_gather_object(handles, bytes(handle), group=group)
+            blob = b"".join(handles)
+            check(lib().tla_exchange_connect(self.handle, ctypes.c_char_p(blob)), "tla_exchange_connect")
+
+    def buffer(self):
+        p = ctypes.c_void_p()
+        check(lib().tla_exchange_buffer(self.handle, ctypes.byref(p)), "tla_exchange_buffer")
+        return p.value
+
+    def connect_buffers(self, buffers):
+        """Connect with device pointers of every rank's buffer (ranks that share one process)."""
+        arr = (ctypes.c_void_p * len(buffers))(*buffers)
+        check(lib().tla_exchange_connect_buffers(self.handle, arr), "tla_exchange_connect_buffers")
+
+    def combine(self, partial, out, gate=None, stream=None):
+        """partial [B, Hq, D+2] float32 -> out [B, Hq*D] (float16 or float32), merged over all ranks."""
+        B, H, D2 = partial.shape
+        flags = _abi.FLAG_IO_FP32 if out.dtype == torch.float32 else 0
+        check(lib().tla_exchange_combine(self.handle, _ptr(partial), B, H, D2 - 2, _ptr(gate), _ptr(out), flags,
+                                         _stream(stream)), "tla_exchange_combine")
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().tla_exchange_destroy(self.handle)
+            self.handle = None
+
+
 class SequenceShardedDecode:
     """One layer of long-context decode sharded by token blocks.
 
-    step(): tla_decode_partial on this rank's block -> all-gather of the
-    (m, l, o) triples over the process group -> tla_combine_lse. Every rank
-    ends with the full output [B, Hq*D] (fp16). All ranks take the same
-    collective steps in the same order.
+    step(): tla_decode_partial on this rank's block, then the (m, l, o)
+    triples of all ranks are merged: exchange="nccl" all-gathers them over the
+    process group and runs tla_combine_lse; exchange="p2p" hands them to a
+    PeerExchange (one kernel: NVLink stores, bounded flag wait, merge). Every
+    rank ends with the full output [B, Hq*D] (fp16). All ranks take the same
+    steps in the same order.
     """
 
     def __init__(self, head_count, kv_head_count, head_dim, total_tokens, rank, world, options=None, batch=1,
-                 group=None):
+                 group=None, exchange="nccl", peer_exchange=None):
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.shard = sequence_shard(total_tokens, world, rank)
         self.world, self.rank, self.group = world, rank, group
         self.capacity = self.shard.tokens + (1 if self.shard.owns_next else 0)
@@ -83,6 +148,13 @@ class SequenceShardedDecode:
         self.partial = torch.empty(batch, head_count, head_dim + 2, dtype=torch.float32, device=dev)
         self.gathered = torch.empty(world, batch, head_count, head_dim + 2, dtype=torch.float32, device=dev)
         self.out = torch.empty(batch, head_count * head_dim, dtype=torch.float16, device=dev)
+        self.exchange = None
+        self.owns_exchange = False
+        if exchange == "p2p" and world > 1:
+            # one PeerExchange can serve every layer of a model (same triple size)
+            self.exchange = peer_exchange or PeerExchange(rank, world, self.partial.numel() * 4, dev, group,
+                                                          self.layer.context)
+            self.owns_exchange = peer_exchange is None
 
     def step(self, qkv, positions, stream=None):
         """qkv [B, (Hq+2Hk)*D] fp16 (identical on every rank); positions int32 [B] (global)."""
@@ -90,9 +162,17 @@ class SequenceShardedDecode:
         local = s.tokens + (1 if s.owns_next else 0)
         self.layer.decode_partial(qkv, positions, s.slot_offset, local, s.owns_next, partial=self.partial,
                                   stream=stream)
+        if self.exchange is not None:
+            return self.exchange.combine(self.partial, self.out, stream=stream)
         if self.world > 1:
             torch.distributed.all_gather_into_tensor(self.gathered.view(-1), self.partial.view(-1), group=self.group)
             parts = self.gathered
         else:
             parts = self.partial.unsqueeze(0)
         return combine_lse(parts, out=self.out, stream=stream)
+
+    def close(self):
+        if self.owns_exchange and self.exchange is not None:
+            self.exchange.close()
+        self.exchange = None
+        self.layer.close()
