@@ -639,32 +639,43 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
 }
 
 // Deferred merge for pairs split across many CTAs (few, long sequences): one
-// block per (pair, query row), one thread per output element; the segment
-// maxima and sums are block reductions and each thread's loop over segments
-// issues independent loads. Pairs covered by a single CTA were written by the
-// decode kernel and are skipped.
+// block per (pair, query row), one thread per output element. The segment
+// table (scratch slot and weight of every contributing CTA) is built once in
+// shared memory, so the output loop's loads have no address dependences and
+// issue back to back; the maxima and sums are block reductions. Pairs covered
+// by a single CTA were written by the decode kernel and are skipped.
+constexpr int kMaxGrid = 16 * 128;  // the host keeps decode_grid <= 16 * D
+
 template <int D, typename IO>
 __global__ void __launch_bounds__(D) decode_merge_kernel(const __grid_constant__ DecodeParams p, int grid) {
   __shared__ long long prefix[kMaxBatch + 1];
+  __shared__ int seg_slot[kMaxGrid];   // scratch slot of segment k, -1 if none
+  __shared__ float seg_w[kMaxGrid];    // segment max, then its weight 2^(m - M)
+  __shared__ float seg_l[kMaxGrid];    // segment sum
   __shared__ float red[2][D / 32];
   const LayerArgs& a = p.a;
   const int G = a.G, Hk = a.Hk;
   const int pair = blockIdx.x / G, r = blockIdx.x - pair * G;
   const int b = pair / Hk, kvh = pair - b * Hk;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) {  // the decode kernel's partition, recomputed (the batch is small on this path)
+  // the decode kernel's partition, recomputed: tile counts in parallel, then a serial scan
+  for (int bb = tid; bb < p.batch; bb += D) {
+    const int pos = p.positions[bb];
+    int lo, hi;
+    seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
+    const bool ok = pos >= 0 && (p.partial_out != nullptr || pos < a.max_tokens) &&
+                    (!p.append || (pos - p.slot_offset >= 0 && pos - p.slot_offset < a.max_tokens &&
+                                   pos - p.slot_offset == hi));
+    prefix[bb + 1] = (ok && hi >= lo) ? static_cast<long long>((hi - lo + kTile) / kTile) * Hk : 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
     long long acc = 0;
-    for (int bb = 0; bb < p.batch; ++bb) {
+    prefix[0] = 0;
+    for (int bb = 1; bb <= p.batch; ++bb) {
+      acc += prefix[bb];
       prefix[bb] = acc;
-      const int pos = p.positions[bb];
-      int lo, hi;
-      seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
-      const bool ok = pos >= 0 && (p.partial_out != nullptr || pos < a.max_tokens) &&
-                      (!p.append || (pos - p.slot_offset >= 0 && pos - p.slot_offset < a.max_tokens &&
-                                     pos - p.slot_offset == hi));
-      acc += (ok && hi >= lo) ? static_cast<long long>((hi - lo + kTile) / kTile) * Hk : 0;
     }
-    prefix[p.batch] = acc;
   }
   __syncthreads();
   const long long total = prefix[p.batch];
@@ -673,15 +684,22 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(const __grid_constant__
   const long long pb = prefix[b] + static_cast<long long>(kvh) * tiles;
   const int c0 = cta_of(pb, total, grid), c1 = cta_of(pb + tiles - 1, total, grid);
   if (c0 == c1) return;  // one CTA held the whole pair
-  auto seg = [&](int c) -> const float* {
-    const long long cb = cta_begin(c, total, grid);
-    if (cta_begin(c + 1, total, grid) == cb) return nullptr;
-    return p.scratch + ((static_cast<size_t>(c) * 2 + (cb >= pb ? 0 : 1)) * G + r) * (D + 2);
-  };
+  const int S = c1 - c0 + 1;
   float m = -INFINITY;
-  for (int c = c0 + tid; c <= c1; c += D) {
-    const float* sp = seg(c);
-    if (sp) m = fmaxf(m, sp[0]);
+  for (int k = tid; k < S; k += D) {
+    const int c = c0 + k;
+    const long long cb = cta_begin(c, total, grid);
+    const int sl = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
+    seg_slot[k] = sl;
+    float mk = -INFINITY, lk = 0.f;
+    if (sl >= 0) {
+      const float* sp = p.scratch + (static_cast<size_t>(sl) * G + r) * (D + 2);
+      mk = __ldcg(sp);
+      lk = __ldcg(sp + 1);
+    }
+    seg_w[k] = mk;
+    seg_l[k] = lk;
+    m = fmaxf(m, mk);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -691,9 +709,10 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(const __grid_constant__
 #pragma unroll
   for (int w = 1; w < D / 32; ++w) M = fmaxf(M, red[0][w]);
   float l = 0.f;
-  for (int c = c0 + tid; c <= c1; c += D) {
-    const float* sp = seg(c);
-    if (sp) l += sp[1] * ex2(sp[0] - M);
+  for (int k = tid; k < S; k += D) {
+    const float w = (seg_slot[k] < 0 || M == -INFINITY) ? 0.f : ex2(seg_w[k] - M);
+    seg_w[k] = w;
+    l += seg_l[k] * w;
   }
   l = warp_sum(l);
   if (lane == 0) red[1][warp] = l;
@@ -701,12 +720,28 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(const __grid_constant__
   float L = 0.f;
 #pragma unroll
   for (int w = 0; w < D / 32; ++w) L += red[1][w];
-  float acc = 0.f;
-#pragma unroll 8
-  for (int c = c0; c <= c1; ++c) {
-    const float* sp = seg(c);
-    if (sp) acc += sp[2 + tid] * ex2(sp[0] - M);
+  const float* col = p.scratch + static_cast<size_t>(r) * (D + 2) + 2 + tid;
+  const size_t slot_stride = static_cast<size_t>(G) * (D + 2);
+  float acc0 = 0.f, acc1 = 0.f;
+  int k = 0;
+  for (; k + 8 <= S; k += 8) {  // eight independent loads in flight per thread
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int sl = seg_slot[k + u];
+      v[u] = sl >= 0 ? __ldcg(col + static_cast<size_t>(sl) * slot_stride) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u += 2) {
+      acc0 += v[u] * seg_w[k + u];
+      acc1 += v[u + 1] * seg_w[k + u + 1];
+    }
   }
+  for (; k < S; ++k) {
+    const int sl = seg_slot[k];
+    if (sl >= 0) acc0 += __ldcg(col + static_cast<size_t>(sl) * slot_stride) * seg_w[k];
+  }
+  const float acc = acc0 + acc1;
   const size_t hrow = static_cast<size_t>(b) * a.Hq + kvh * G + r;
   if (p.partial_out) {
     p.partial_out[hrow * (D + 2) + 2 + tid] = acc;
