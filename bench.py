@@ -225,8 +225,12 @@ class Ragged8B(Decode1B):
         self.bytes_per_step = L * per_layer
         self.bytes_per_launch = per_layer
         self.tokens_per_step = B / world  # a rank computes its heads of every sequence
-        self.launches_per_step = L
-        self.kernel = "decode_fast_kernel<128,half>"
+        # the split-KV merge runs as its own kernel when the persistent grid
+        # (2 CTAs per SM) exceeds 4 CTAs per (sequence, kv head) pair
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        deferred = 2 * sms > 4 * B * hk
+        self.launches_per_step = L * (2 if deferred else 1)
+        self.kernel = "decode_fast_kernel<128,half>" + (" + decode_merge_kernel" if deferred else "")
         self.config = {"workload": "ragged_8b (config 4): 32 layers x 32q/8kv heads x d128, fp16 KV, batch 64, "
                                    "context U[512, 8192] (seed 0), theta 5e5", "global_batch": B,
                        "parallelism": f"kv-head groups x{world} ({hk} kv / {hq} q heads per GPU)",
@@ -264,9 +268,9 @@ class LongCtx:
         self.bytes_per_step = L * decode_seq_bytes(T + 1, Hq, Hk, D) / world  # this rank's share
         self.bytes_per_launch = decode_seq_bytes(local, Hq, Hk, D)
         self.tokens_per_step = 1 / world
-        self.launches_per_step = 2 * L
+        self.launches_per_step = (2 if world == 1 else 3) * L  # decode, merge (+ exchange or combine)
         if world == 1:
-            self.kernel = "decode_fast_kernel<128,half> partial + combine_lse_kernel"
+            self.kernel = "decode_fast_kernel<128,half> + decode_merge_kernel (one shard: plain decode)"
             xname = "none"
         elif mode == "p2p":
             self.kernel = "decode_fast_kernel<128,half> partial + exchange_combine_kernel (NVLink stores + merge)"

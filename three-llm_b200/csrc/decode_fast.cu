@@ -639,27 +639,33 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
 }
 
 // Deferred merge for pairs split across many CTAs (few, long sequences): one
-// block per (pair, query row), one thread per output element. The segment
-// table (scratch slot and weight of every contributing CTA) is built once in
-// shared memory, so the output loop's loads have no address dependences and
-// issue back to back; the maxima and sums are block reductions. Pairs covered
-// by a single CTA were written by the decode kernel and are skipped.
+// block of 4 warps per (pair, query row). The segment table (scratch slot and
+// weight of every contributing CTA) is built once in shared memory; then warp
+// w sums segments w, w + 4, ... with each lane holding D / 32 output columns,
+// eight segments' loads in flight at a time, and the four partial rows are
+// added through shared memory. Pairs covered by a single CTA were written by
+// the decode kernel and are skipped.
 constexpr int kMaxGrid = 16 * 128;  // the host keeps decode_grid <= 16 * D
+constexpr int kMergeThreads = 128;
 
 template <int D, typename IO>
-__global__ void __launch_bounds__(D) decode_merge_kernel(const __grid_constant__ DecodeParams p, int grid) {
+__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const __grid_constant__ DecodeParams p,
+                                                                     int grid) {
+  constexpr int kWarps = kMergeThreads / 32;
+  constexpr int kPer = D / 32;  // output columns per lane (float2 loads)
   __shared__ long long prefix[kMaxBatch + 1];
   __shared__ int seg_slot[kMaxGrid];   // scratch slot of segment k, -1 if none
   __shared__ float seg_w[kMaxGrid];    // segment max, then its weight 2^(m - M)
   __shared__ float seg_l[kMaxGrid];    // segment sum
-  __shared__ float red[2][D / 32];
+  __shared__ float red[2][kWarps];
+  __shared__ float rows_s[kWarps][D];
   const LayerArgs& a = p.a;
   const int G = a.G, Hk = a.Hk;
   const int pair = blockIdx.x / G, r = blockIdx.x - pair * G;
   const int b = pair / Hk, kvh = pair - b * Hk;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // the decode kernel's partition, recomputed: tile counts in parallel, then a serial scan
-  for (int bb = tid; bb < p.batch; bb += D) {
+  for (int bb = tid; bb < p.batch; bb += kMergeThreads) {
     const int pos = p.positions[bb];
     int lo, hi;
     seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
@@ -686,7 +692,7 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(const __grid_constant__
   if (c0 == c1) return;  // one CTA held the whole pair
   const int S = c1 - c0 + 1;
   float m = -INFINITY;
-  for (int k = tid; k < S; k += D) {
+  for (int k = tid; k < S; k += kMergeThreads) {
     const int c = c0 + k;
     const long long cb = cta_begin(c, total, grid);
     const int sl = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
@@ -707,9 +713,9 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(const __grid_constant__
   __syncthreads();
   float M = red[0][0];
 #pragma unroll
-  for (int w = 1; w < D / 32; ++w) M = fmaxf(M, red[0][w]);
+  for (int w = 1; w < kWarps; ++w) M = fmaxf(M, red[0][w]);
   float l = 0.f;
-  for (int k = tid; k < S; k += D) {
+  for (int k = tid; k < S; k += kMergeThreads) {
     const float w = (seg_slot[k] < 0 || M == -INFINITY) ? 0.f : ex2(seg_w[k] - M);
     seg_w[k] = w;
     l += seg_l[k] * w;
@@ -719,41 +725,67 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(const __grid_constant__
   __syncthreads();
   float L = 0.f;
 #pragma unroll
-  for (int w = 0; w < D / 32; ++w) L += red[1][w];
-  const float* col = p.scratch + static_cast<size_t>(r) * (D + 2) + 2 + tid;
-  const size_t slot_stride = static_cast<size_t>(G) * (D + 2);
-  float acc0 = 0.f, acc1 = 0.f;
-  int k = 0;
-  for (; k + 8 <= S; k += 8) {  // eight independent loads in flight per thread
-    float v[8];
+  for (int w = 0; w < kWarps; ++w) L += red[1][w];
+  // rows are (D + 2) floats: 8-byte aligned, so float2 loads
+  const float2* col = reinterpret_cast<const float2*>(p.scratch + static_cast<size_t>(r) * (D + 2) + 2) + lane;
+  const size_t slot_stride2 = static_cast<size_t>(G) * (D + 2) / 2;
+  float2 acc[kPer / 2];
+#pragma unroll
+  for (int j = 0; j < kPer / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+  int k = warp;
+  for (; k + 7 * kWarps < S; k += 8 * kWarps) {  // eight segments' loads in flight
+    float2 v[8][kPer / 2];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const int sl = seg_slot[k + u];
-      v[u] = sl >= 0 ? __ldcg(col + static_cast<size_t>(sl) * slot_stride) : 0.f;
+      const int sl = seg_slot[k + u * kWarps];
+#pragma unroll
+      for (int j = 0; j < kPer / 2; ++j)
+        v[u][j] = sl >= 0 ? __ldcg(col + static_cast<size_t>(sl) * slot_stride2 + j * 32) : make_float2(0.f, 0.f);
     }
 #pragma unroll
-    for (int u = 0; u < 8; u += 2) {
-      acc0 += v[u] * seg_w[k + u];
-      acc1 += v[u + 1] * seg_w[k + u + 1];
+    for (int u = 0; u < 8; ++u) {
+      const float w = seg_w[k + u * kWarps];
+#pragma unroll
+      for (int j = 0; j < kPer / 2; ++j) {
+        acc[j].x += v[u][j].x * w;
+        acc[j].y += v[u][j].y * w;
+      }
     }
   }
-  for (; k < S; ++k) {
+  for (; k < S; k += kWarps) {
     const int sl = seg_slot[k];
-    if (sl >= 0) acc0 += __ldcg(col + static_cast<size_t>(sl) * slot_stride) * seg_w[k];
-  }
-  const float acc = acc0 + acc1;
-  const size_t hrow = static_cast<size_t>(b) * a.Hq + kvh * G + r;
-  if (p.partial_out) {
-    p.partial_out[hrow * (D + 2) + 2 + tid] = acc;
-    if (tid == 0) {
-      p.partial_out[hrow * (D + 2)] = M;
-      p.partial_out[hrow * (D + 2) + 1] = L;
+    if (sl < 0) continue;
+    const float w = seg_w[k];
+#pragma unroll
+    for (int j = 0; j < kPer / 2; ++j) {
+      const float2 v = __ldcg(col + static_cast<size_t>(sl) * slot_stride2 + j * 32);
+      acc[j].x += v.x * w;
+      acc[j].y += v.y * w;
     }
-  } else {
-    float val = acc / L;
-    const size_t oi = hrow * D + tid;
-    if (p.gate) val = val * (1.f / (1.f + expf(-to_f32(static_cast<const IO*>(p.gate)[oi]))));
-    static_cast<IO*>(p.out)[oi] = from_f32<IO>(val);
+  }
+#pragma unroll
+  for (int j = 0; j < kPer / 2; ++j) {
+    rows_s[warp][2 * (lane + 32 * j)] = acc[j].x;
+    rows_s[warp][2 * (lane + 32 * j) + 1] = acc[j].y;
+  }
+  __syncthreads();
+  const size_t hrow = static_cast<size_t>(b) * a.Hq + kvh * G + r;
+  for (int d = tid; d < D; d += kMergeThreads) {
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) o += rows_s[w][d];
+    if (p.partial_out) {
+      p.partial_out[hrow * (D + 2) + 2 + d] = o;
+      if (d == 0) {
+        p.partial_out[hrow * (D + 2)] = M;
+        p.partial_out[hrow * (D + 2) + 1] = L;
+      }
+    } else {
+      float val = o / L;
+      const size_t oi = hrow * D + d;
+      if (p.gate) val = val * (1.f / (1.f + expf(-to_f32(static_cast<const IO*>(p.gate)[oi]))));
+      static_cast<IO*>(p.out)[oi] = from_f32<IO>(val);
+    }
   }
 }
 
@@ -763,7 +795,7 @@ cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, cudaStream_t str
   decode_fast_kernel<D, IO, TWO><<<L->decode_grid, kThreads, s.total, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !p.defer_merge) return e;
-  decode_merge_kernel<D, IO><<<p.batch * L->Hk * L->G, D, 0, stream>>>(p, L->decode_grid);
+  decode_merge_kernel<D, IO><<<p.batch * L->Hk * L->G, kMergeThreads, 0, stream>>>(p, L->decode_grid);
   return cudaGetLastError();
 }
 

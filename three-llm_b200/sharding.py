@@ -158,6 +158,8 @@ class SequenceShardedDecode:
 
     def step(self, qkv, positions, stream=None):
         """qkv [B, (Hq+2Hk)*D] fp16 (identical on every rank); positions int32 [B] (global)."""
+        if self.world == 1:  # one shard holds the whole sequence: a plain decode step
+            return self.layer.decode(qkv.view(self.B, -1), positions, out=self.out, stream=stream)
         s = self.shard
         local = s.tokens + (1 if s.owns_next else 0)
         self.layer.decode_partial(qkv, positions, s.slot_offset, local, s.owns_next, partial=self.partial,
