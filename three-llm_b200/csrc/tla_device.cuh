@@ -56,11 +56,56 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Waits for the phase with the given parity; false (and TLA_ERR_TIMEOUT in
 // *err) if it did not complete within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity);
+// The clock is read once every 64 polls: a waiting thread shares its
+// sub-partition's issue slots with the compute warps, so its loop is kept short.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;  // already complete: no suspend round trip
   const unsigned long long t0 = globaltimer();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      report_error(err, TLA_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Non-blocking test of a phase (no suspension), and a bounded spin on it for
+// the single-thread issuers whose next step is already due most of the time.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      report_error(err, TLA_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Bounded poll with a short sleep between tests: for a single issuing thread
+// whose sub-partition also runs issue-heavy warps.
+__device__ __forceinline__ bool mbar_nap(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    __nanosleep(64);
+    if (mbar_test_wait(bar, parity)) return true;
     if (globaltimer() - t0 > kWaitLimitNs) {
       report_error(err, TLA_ERR_TIMEOUT);
       return false;
@@ -107,6 +152,13 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // 2^x with the hardware approximation (MUFU.EX2).

@@ -48,7 +48,7 @@ struct tla_layer {
   // tensor-core prefill path (cache maps with 128-token boxes)
   bool fast_prefill = false;
   size_t prefill_smem = 0;
-  CUtensorMap tmap_k128{}, tmap_v128{};
+  CUtensorMap tmap_k128{}, tmap_v128{};  // 128-token boxes
 };
 
 namespace tla {
