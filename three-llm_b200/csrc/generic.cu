@@ -362,6 +362,126 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(LayerArgs a, cons
   }
 }
 
+// fp16 rows, head_dim 64 or 128: a warp per token, each lane owns 16 bytes
+// (8 dims) of a head, so one warp-wide load covers 32 / (D / 8) heads and the
+// whole qkv row is in flight in a few loads; the rotate-half partner is
+// (rotary / 16) lanes away (a power of two: xor shuffle within the head's
+// lane group), RMS norms reduce over the group, and cos/sin are computed once
+// per token (lane k: pairs k and k + 32) and gathered by shuffles.
+template <int D>
+__global__ void __launch_bounds__(128) rope_rows_kernel(LayerArgs a, const __half* __restrict__ qkv,
+                                                        const int32_t* __restrict__ start, int seq_len, int tokens,
+                                                        __half* __restrict__ qscr) {
+  constexpr int L = D / 8;     // lanes per head
+  constexpr int HPW = 32 / L;  // heads per warp-wide load
+  constexpr int kLoads = 8;    // warp-wide loads in flight per round
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int ti = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (ti >= tokens) return;
+  const int b = ti / seq_len, t = ti - b * seq_len;
+  const int Hq = a.Hq, Hk = a.Hk, heads = Hq + 2 * Hk;
+  const int g = lane / L, d0 = 8 * (lane % L);
+  const __half* row = qkv + static_cast<size_t>(ti) * heads * D;
+  // the first round of loads goes out before the position is known
+  uint4 raw[kLoads];
+#pragma unroll
+  for (int c = 0; c < kLoads; ++c) {
+    const int hh = c * HPW + g;
+    raw[c] = hh < heads ? *reinterpret_cast<const uint4*>(row + hh * D + d0) : make_uint4(0, 0, 0, 0);
+  }
+  const int pos = start[b] + t;
+  if (pos < 0 || pos >= a.max_tokens) {
+    if (lane == 0) report_error(a.error, TLA_ERR_POSITION);
+    return;
+  }
+  const int half = a.rotary / 2, hl = half / 8;
+  const bool rot = d0 < a.rotary, lo_side = d0 < half;
+  float c0 = 1.f, s0 = 0.f, c1 = 1.f, s1 = 0.f;
+  if (lane < a.pair_count && lane < half) rope_cos_sin(pos, a.inv_freq[lane], &c0, &s0);
+  if (lane + 32 < a.pair_count && lane + 32 < half) rope_cos_sin(pos, a.inv_freq[lane + 32], &c1, &s1);
+  float cs[8], sn[8];
+  bool turn[8];
+  const int jb = lo_side ? d0 : d0 - half;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int j = jb + e, src = j & 31;
+    const float cc0 = __shfl_sync(full, c0, src), ss0 = __shfl_sync(full, s0, src);
+    const float cc1 = __shfl_sync(full, c1, src), ss1 = __shfl_sync(full, s1, src);
+    turn[e] = rot && j < a.pair_count;
+    cs[e] = j < 32 ? cc0 : cc1;
+    sn[e] = j < 32 ? ss0 : ss1;
+  }
+  __half* kc = static_cast<__half*>(a.k_cache);
+  __half* vc = static_cast<__half*>(a.v_cache);
+  for (int h0 = 0; h0 < heads; h0 += kLoads * HPW) {
+    if (h0 > 0) {
+#pragma unroll
+      for (int c = 0; c < kLoads; ++c) {
+        const int hh = h0 + c * HPW + g;
+        raw[c] = hh < heads ? *reinterpret_cast<const uint4*>(row + hh * D + d0) : make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kLoads; ++c) {
+      if (h0 + c * HPW >= heads) break;  // warp-uniform
+      const int hh = h0 + c * HPW + g;
+      float x[8];
+      const __half2* hp = reinterpret_cast<const __half2*>(&raw[c]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        x[2 * e] = __low2float(hp[e]);
+        x[2 * e + 1] = __high2float(hp[e]);
+      }
+      const float* w = hh < Hq ? a.q_norm : (hh < Hq + Hk ? a.k_norm : nullptr);
+      const bool norm = hh < Hq + Hk ? w != nullptr : a.v_norm != 0;
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
+#pragma unroll
+      for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(full, ss, o);
+      if (norm) {  // math.ts:78-97
+        const float inv_rms = 1.f / sqrtf(ss / static_cast<float>(D) + a.rms_eps);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float sc = w == nullptr ? 1.f : (a.offset_rms ? 1.f + w[d0 + e] : w[d0 + e]);
+          x[e] = x[e] * inv_rms * sc;
+        }
+      }
+      float pt[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pt[e] = __shfl_xor_sync(full, x[e], hl);
+      if (hh < Hq + Hk) {  // RoPE, math.ts:134-147
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (turn[e]) x[e] = (x[e] * cs[e] + (lo_side ? -pt[e] : pt[e]) * sn[e]) * a.attn_factor;
+      }
+      if (hh >= heads) continue;
+      uint4 outv;
+      uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ov[e] = pack_half2(x[2 * e], x[2 * e + 1]);
+      __half* dst;
+      if (hh < Hq)
+        dst = qscr + ((static_cast<size_t>(b) * Hq + hh) * seq_len + t) * D + d0;
+      else if (hh < Hq + Hk)
+        dst = kc + ((static_cast<size_t>(b) * Hk + (hh - Hq)) * a.max_tokens + pos) * D + d0;
+      else
+        dst = vc + ((static_cast<size_t>(b) * Hk + (hh - Hq - Hk)) * a.max_tokens + pos) * D + d0;
+      *reinterpret_cast<uint4*>(dst) = outv;
+    }
+  }
+}
+
+template <int D>
+cudaError_t rope_rows_t(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
+                        __half* qscr, cudaStream_t stream) {
+  const int tokens = batch * seq_len;
+  rope_rows_kernel<D><<<(tokens + 3) / 4, 128, 0, stream>>>(layer_args(L), static_cast<const __half*>(qkv), start,
+                                                            seq_len, tokens, qscr);
+  return cudaGetLastError();
+}
+
 template <typename IO, int D>
 cudaError_t rope_warp_t(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
                         __half* qscr, cudaStream_t stream) {
@@ -375,6 +495,10 @@ cudaError_t launch_rope_append_half_q(const tla_layer* L, const void* qkv, const
                                       int seq_len, __half* qscr, cudaStream_t stream) {
   const int epl = L->D / 32;
   const bool warp_ok = !L->cache_fp32 && (L->D == 64 || L->D == 128) && ((L->rotary / 2) % epl == 0);
+  const int hl = L->rotary / 16;
+  const bool rows_ok = warp_ok && !L->io_fp32 && (L->rotary / 2) % 8 == 0 && (hl & (hl - 1)) == 0;
+  if (rows_ok) return L->D == 64 ? rope_rows_t<64>(L, qkv, start, batch, seq_len, qscr, stream)
+                                 : rope_rows_t<128>(L, qkv, start, batch, seq_len, qscr, stream);
   if (warp_ok) {
     if (L->D == 64)
       return L->io_fp32 ? rope_warp_t<float, 64>(L, qkv, start, batch, seq_len, qscr, stream)
