@@ -163,28 +163,37 @@ __device__ __forceinline__ void tmem_ld64x(uint32_t taddr, uint32_t (&r)[64]) {
 }
 
 // ---------------------------------------------------------------- the kernel
-// One 128-row query tile of one (head, sequence) per CTA, K/V in 128-token
-// steps. The tcgen05 pipe runs one MMA at a time and the issuing thread waits
-// for each to be accepted, so the issuer's instruction stream is the tensor
-// timeline. Three TMEM S buffers let it run S three steps ahead of P V: the
-// issue order is S(0) S(1) S(2) PV(0) S(3) PV(1) S(4) ..., so S(n) is long
-// finished when the softmax warpgroup reaches step n, and the issuer only
-// ever waits for a softmax step before its P V. N = 128 for the S MMAs (full
-// rate) and N = head_dim for P V.
+// Persistent: one CTA per SM walks a fixed list of work items, an item being
+// one 128-row query tile of one (head, sequence), K/V in 128-token steps.
+// Items are ordered longest first and dealt to the CTAs in snake order
+// (c, 2G-1-c, 2G+c, ...), so every CTA gets a similar amount of work; the
+// step counter g runs across a CTA's items, so the TMA rings, the S buffers
+// and the barriers flow from one item into the next without a drain, and the
+// next item's Q load and first S MMAs overlap the current item's epilogue.
+//
+// The tcgen05 pipe runs one MMA at a time and the issuing thread waits for
+// each to be accepted, so the issuer's instruction stream is the tensor
+// timeline. NS TMEM S buffers let it run S NS steps ahead of P V: the issue
+// order is S(0) .. S(NS-1) PV(0) S(NS) PV(1) ..., so S(g) is long finished
+// when the softmax warpgroup reaches step g, and the issuer only ever waits
+// for a softmax step before its P V. N = 128 for the S MMAs (full rate) and
+// N = head_dim for P V.
 // Softmax thread = one query row (TMEM lane), all 128 columns of the step in
-// registers (one pass). P(n) is written as fp16 pairs over the first 64
+// registers (one pass). P(g) is written as fp16 pairs over the first 64
 // columns of its own S buffer and read from there as the A operand of P V;
-// S(n+3) reuses the buffer only after P V(n) was issued. (Splitting the
+// S(g+NS) reuses the buffer only after P V(g) was issued. (Splitting the
 // columns over two warps per sub-partition, with a per-step exchange of the
-// row maxima, measured slower.) O accumulates in
-// TMEM; a row's reference maximum only moves when a step's maximum exceeds it
-// by more than 2^8 (O is then rescaled in TMEM after the previous P V
-// finished), so P stays <= 256 in fp16.
-// P V(n) completion is signalled on o_done[n & 1]. A softmax thread can be up
+// row maxima, measured slower.) O accumulates in TMEM, double-buffered by
+// item where TMEM has room (head_dim 64), so the next item's P V can start
+// before this item's epilogue has read its O (o_free); likewise the Q tile in
+// shared memory (head_dim 64; at 128 the K/V stages take the room). A row's reference maximum only moves when a step's maximum
+// exceeds it by more than 2^8 (O is then rescaled in TMEM after the previous
+// P V finished), so P stays <= 256 in fp16.
+// P V(g) completion is signalled on o_done[g & 1]. A softmax thread can be up
 // to two P V steps behind the issuer, which one barrier's phase parity cannot
-// tell apart; with two barriers, and the softmax waiting for P V(n-2) at every
-// step n, each barrier is at most one phase from any phase a thread waits for.
-// TMEM columns: S/P buffer j at 128 j (j < 3), O at 384.
+// tell apart; with two barriers, and the softmax waiting for P V(g-2) at every
+// step g, each barrier is at most one phase from any phase a thread waits for.
+// TMEM columns: S/P buffer j at 128 j (j < NS), O buffer i at 128 NS + D i (i < NO).
 constexpr int kThreads = 192;  // warps 0-3: softmax, 4: TMA, 5: MMA
 constexpr int kMmaWarp = 5, kTmaWarp = 4;
 
@@ -193,61 +202,89 @@ struct PCfg {
   static constexpr int kBoxes = D / 64;
   static constexpr int kBox = 128 * 128;         // [128 rows][64 fp16]
   static constexpr int kTile = kBoxes * kBox;    // Q tile, or K (V) of one step
+  static constexpr int kNS = 3;                  // TMEM S buffers
+  static constexpr int kNO = D == 64 ? 2 : 1;    // TMEM O buffers (by item)
+  static constexpr int kNQ = D == 64 ? 2 : 1;    // Q tiles in shared memory (by item)
   static constexpr int kST = D == 64 ? 4 : 3;    // K/V stages (K and V rings are filled independently)
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kTile;
+  static constexpr int kK = kQ + kNQ * kTile;
   static constexpr int kV = kK + kST * kTile;
   static constexpr int kBar = kV + kST * kTile;
-  // q_full; k_full, v_full, k_empty, v_empty [kST]; s_full [3]; p_full [3]; o_done [2]
-  static constexpr int kNumBars = 1 + 4 * kST + 3 + 3 + 2;
+  // q_full, q_empty [2]; k_full, v_full, k_empty, v_empty [kST]; s_full, p_full [kNS]; o_done, o_free [2]
+  static constexpr int kNumBars = 4 + 4 * kST + 2 * kNS + 4;
   static constexpr int kSmem = kBar + kNumBars * 8 + 16 + 1024;
-  static constexpr uint32_t kO = 384, kCols = 512;
+  static constexpr uint32_t kO = 128 * kNS, kCols = 512;
+  static_assert(kO + kNO * D <= kCols, "TMEM columns");
 };
+
+// A work item and its step range: item it (longest first) -> query tile m of
+// (sequence b, head h); the tile's steps are the 128-token KV tiles j0 .. j0+N-1.
+struct PrefillItem {
+  int b, h, row0, rows, j0, N, start;
+};
+
+__device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int it) {
+  PrefillItem w;
+  const int bh_count = p.batch * p.Hq;
+  const int m = p.num_m - 1 - it / bh_count;
+  const int bh = it % bh_count;
+  w.b = bh / p.Hq;
+  w.h = bh - w.b * p.Hq;
+  w.start = p.start[w.b];
+  w.row0 = m * 128;
+  w.rows = min(128, p.S - w.row0);
+  const int first_min = p.sliding > 0 ? max(0, w.start + w.row0 - p.sliding + 1) : 0;
+  w.j0 = first_min / 128;
+  w.N = (w.start + w.row0 + w.rows - 1) / 128 - w.j0 + 1;
+  return w;
+}
+
+// Item index of this CTA's k-th item (snake order over the grid), or -1.
+__device__ __forceinline__ int prefill_item_of(int k, int num_items) {
+  const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+  const int it = k * G + ((k & 1) ? G - 1 - c : c);
+  return it < num_items ? it : -1;
+}
 
 template <int D, typename OUT>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
   using C = PCfg<D>;
-  constexpr int kT = 128;
+  constexpr int kT = 128, NS = C::kNS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
+  uint64_t* q_full = bars;  // [item % NQ]
+  uint64_t* q_empty = bars + 2;
+  uint64_t* k_full = bars + 4;
   uint64_t* v_full = k_full + C::kST;
   uint64_t* k_empty = v_full + C::kST;
   uint64_t* v_empty = k_empty + C::kST;
-  uint64_t* s_full = v_empty + C::kST;  // [j]
-  uint64_t* p_full = s_full + 3;        // [j]
-  uint64_t* o_done = p_full + 3;        // [n & 1]
+  uint64_t* s_full = v_empty + C::kST;  // [g % NS]
+  uint64_t* p_full = s_full + NS;       // [g % NS]
+  uint64_t* o_done = p_full + NS;       // [g & 1]
+  uint64_t* o_free = o_done + 2;        // [item % NO]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  const int bh_count = p.batch * p.Hq;
-  const int m = p.num_m - 1 - static_cast<int>(blockIdx.x) / bh_count;  // 128-row tile, longest first
-  const int bh = static_cast<int>(blockIdx.x) % bh_count;
-  const int b = bh / p.Hq, h = bh - b * p.Hq, kvh = h / p.G;
-  const int start = p.start[b];
-  const int row0 = m * 128;
-  const int rows = min(128, p.S - row0);
-  const int first_min = p.sliding > 0 ? max(0, start + row0 - p.sliding + 1) : 0;
-  const int j0 = first_min / kT;
-  const int N = (start + row0 + rows - 1) / kT - j0 + 1;
+  const int num_items = p.num_m * p.batch * p.Hq;
 
   if (tid == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&o_free[i], 128);
+    }
     for (int i = 0; i < C::kST; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
     }
-    mbar_init(&o_done[0], 1);
-    mbar_init(&o_done[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -268,34 +305,45 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 
   if (warp == kTmaWarp) {
     // ================================================================ TMA producer
-    // lane 0: Q, then the K ring; lane 1: the V ring. S runs up to three steps
-    // ahead of P V, so K must not queue behind V.
+    // lane 0: Q of each item, then its K tiles; lane 1: the V tiles. S runs
+    // up to NS steps ahead of P V, so K must not queue behind V.
     if (lane < 2) {
-      const int z = b * p.Hk + kvh;
       const CUtensorMap* map = lane == 0 ? &p.tm_k : &p.tm_v;
       uint64_t* full = lane == 0 ? k_full : v_full;
       uint64_t* empty = lane == 0 ? k_empty : v_empty;
       uint8_t* ring = smem + (lane == 0 ? C::kK : C::kV);
       tma_prefetch(map);
-      if (lane == 0) {
-        tma_prefetch(&p.tm_q);
-        mbar_arrive_expect_tx(q_full, C::kTile);
+      if (lane == 0) tma_prefetch(&p.tm_q);
+      int g = 0;
+      for (int k = 0;; ++k) {
+        const int it = prefill_item_of(k, num_items);
+        if (it < 0) break;
+        const PrefillItem w = prefill_item(p, it);
+        const int z = w.b * p.Hk + w.h / p.G;
+        if (lane == 0) {
+          const int qi = k % C::kNQ;
+          wait(&q_empty[qi], ((k / C::kNQ) & 1) ^ 1);
+          if (!*abort_flag) {
+            mbar_arrive_expect_tx(&q_full[qi], C::kTile);
 #pragma unroll
-        for (int x = 0; x < C::kBoxes; ++x)
-          tma_load_3d(smem + C::kQ + x * C::kBox, &p.tm_q, q_full, x * 64, row0, b * p.Hq + h);
-      }
-      for (int n = 0; n < N; ++n) {
-        const int st = n % C::kST;
-        wait(&empty[st], ((n / C::kST) & 1) ^ 1);
-        if (!*abort_flag) {
-          mbar_arrive_expect_tx(&full[st], C::kTile);
+            for (int x = 0; x < C::kBoxes; ++x)
+              tma_load_3d(smem + C::kQ + qi * C::kTile + x * C::kBox, &p.tm_q, &q_full[qi], x * 64, w.row0,
+                          w.b * p.Hq + w.h);
+          }
+        }
+        for (int n = 0; n < w.N; ++n, ++g) {
+          const int st = g % C::kST;
+          wait(&empty[st], ((g / C::kST) & 1) ^ 1);
+          if (!*abort_flag) {
+            mbar_arrive_expect_tx(&full[st], C::kTile);
 #pragma unroll
-          for (int x = 0; x < C::kBoxes; ++x)
-            tma_load_3d(ring + st * C::kTile + x * C::kBox, map, &full[st], x * 64, (j0 + n) * kT, z);
+            for (int x = 0; x < C::kBoxes; ++x)
+              tma_load_3d(ring + st * C::kTile + x * C::kBox, map, &full[st], x * 64, (w.j0 + n) * kT, z);
+          }
         }
       }
-      for (int n = max(0, N - C::kST); n < N; ++n)  // no copies in flight at exit
-        wait(&full[n % C::kST], (n / C::kST) & 1);
+      for (int q = max(0, g - C::kST); q < g; ++q)  // no copies in flight at exit
+        wait(&full[q % C::kST], (q / C::kST) & 1);
     }
   } else if (warp == kMmaWarp) {
     // ================================================================ MMA issuer
@@ -306,157 +354,192 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         if (!*abort_flag && !mbar_spin(bar, parity, p.error)) *abort_flag = 1;
       };
       // Descriptors are linear in the start address (bits 0-13 = addr >> 4, no
-      // carry below 256 KB), so stage, box and k-step offsets are plain adds.
+      // carry below 256 KB), so buffer, stage, box and k-step offsets are plain adds.
       const uint64_t dq = sdesc(smem_u32(smem + C::kQ), 16, 1024);
       const uint64_t dk = sdesc(smem_u32(smem + C::kK), 16, 1024);
       const uint64_t dv = sdesc(smem_u32(smem + C::kV), C::kBox, 1024);
-      auto issue_s = [&](int n) {  // S(n) = Q K(n)^T into buffer n % 3
-        const int st = n % C::kST;
-        spin(&k_full[st], (n / C::kST) & 1);
-        PTRACE(8, n);
+      // S cursor (item ks, local step ns, global step gs) runs NS steps ahead
+      // of the P V cursor (kp, np, gp).
+      int ks = 0, ns = 0, gs = 0, its = prefill_item_of(0, num_items);
+      int Ns = its >= 0 ? prefill_item(p, its).N : 0;
+      auto issue_s = [&]() -> bool {  // S(gs) = Q K(gs)^T into buffer gs % NS; false when no step is left
+        if (its < 0) return false;
+        if (ns == 0) spin(&q_full[ks % C::kNQ], (ks / C::kNQ) & 1);
+        const int st = gs % C::kST;
+        spin(&k_full[st], (gs / C::kST) & 1);
+        PTRACE(8, gs);
+        const uint64_t qb = dq + static_cast<uint64_t>((ks % C::kNQ) * (C::kTile >> 4));
         const uint64_t kb = dk + static_cast<uint64_t>(st * (C::kTile >> 4));
-        const uint32_t d = tmem + 128 * (n % 3);
+        const uint32_t d = tmem + 128 * (gs % NS);
         if (!*abort_flag) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = ((kk >> 2) * C::kBox + (kk & 3) * 32) >> 4;
-            mma_f16(d, dq + off, kb + off, kIdS, kk > 0 ? 1u : 0u);
+            mma_f16(d, qb + off, kb + off, kIdS, kk > 0 ? 1u : 0u);
           }
         }
-        mma_commit(&s_full[n % 3]);
+        mma_commit(&s_full[gs % NS]);
         mma_commit(&k_empty[st]);
-        PTRACE(9, n);
+        PTRACE(9, gs);
+        ++gs;
+        if (++ns == Ns) {  // this item's last S: its Q tile is free
+          mma_commit(&q_empty[ks % C::kNQ]);
+          ns = 0;
+          its = prefill_item_of(++ks, num_items);
+          Ns = its >= 0 ? prefill_item(p, its).N : 0;
+        }
+        return true;
       };
-      spin(q_full, 0);
-      for (int n = 0; n < 3 && n < N; ++n) issue_s(n);
-      for (int n = 0; n < N; ++n) {  // O += P(n) V(n) once the softmax step is done, then S(n + 3)
-        const int st = n % C::kST;
-        spin(&v_full[st], (n / C::kST) & 1);
+      for (int i = 0; i < NS; ++i) issue_s();
+      int kp = 0, np = 0, gp = 0, itp = prefill_item_of(0, num_items);
+      int Np = itp >= 0 ? prefill_item(p, itp).N : 0;
+      while (itp >= 0) {  // O(item) += P(gp) V(gp) once the softmax step is done, then S(gp + NS)
+        const int st = gp % C::kST;
+        if (np == 0 && kp >= C::kNO)  // the epilogue of item kp - NO has read this O buffer
+          spin(&o_free[kp % C::kNO], ((kp / C::kNO) - 1) & 1);
+        spin(&v_full[st], (gp / C::kST) & 1);
         // the softmax step is usually still running: sleep on the barrier
         // instead of spinning, which would take issue slots from the softmax
         // warp on this sub-partition
-        if (!*abort_flag && !mbar_nap(&p_full[n % 3], (n / 3) & 1, p.error)) *abort_flag = 1;
+        wait(&p_full[gp % NS], (gp / NS) & 1);
         tc_fence_after();
-        PTRACE(10, n);
+        PTRACE(10, gp);
         const uint64_t vb = dv + static_cast<uint64_t>(st * (C::kTile >> 4));
-        const uint32_t a = tmem + 128 * (n % 3);
+        const uint32_t a = tmem + 128 * (gp % NS);
+        const uint32_t o = tmem + C::kO + D * (kp % C::kNO);
         if (!*abort_flag) {
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)
-            mma_f16_ts(tmem + C::kO, a + kk * 8, vb + 128 * kk, kIdO, (n > 0 || kk > 0) ? 1u : 0u);
+            mma_f16_ts(o, a + kk * 8, vb + 128 * kk, kIdO, (np > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&o_done[n & 1]);
+        mma_commit(&o_done[gp & 1]);
         mma_commit(&v_empty[st]);
-        PTRACE(11, n);
-        if (n + 3 < N) issue_s(n + 3);
+        PTRACE(11, gp);
+        ++gp;
+        if (++np == Np) {
+          np = 0;
+          itp = prefill_item_of(++kp, num_items);
+          Np = itp >= 0 ? prefill_item(p, itp).N : 0;
+        }
+        issue_s();
       }
     }
   } else {
     // ================================================================ softmax
     const int r = tid;  // query row = TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const uint32_t o_addr = lane_addr + C::kO;
-    const int pr = start + row0 + r;
-    const int first_r = p.sliding > 0 ? max(0, pr - p.sliding + 1) : 0;
     const float sl2 = p.scale_log2;
-    float m_run = -INFINITY, l_run = 0.f;
-    for (int n = 0; n < N; ++n) {
-      const int j = n % 3;
-      const uint32_t buf = lane_addr + 128 * j;
-      wait(&s_full[j], (n / 3) & 1);
-      if (n >= 2) wait(&o_done[n & 1], ((n - 2) >> 1) & 1);  // P V(n-2): keeps o_done within one phase
+    int g = 0;
+    for (int k = 0;; ++k) {
+      const int it = prefill_item_of(k, num_items);
+      if (it < 0) break;
+      const PrefillItem w = prefill_item(p, it);
+      const uint32_t o_addr = lane_addr + C::kO + D * (k % C::kNO);
+      const int pr = w.start + w.row0 + r;
+      const int first_r = p.sliding > 0 ? max(0, pr - p.sliding + 1) : 0;
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int n = 0; n < w.N; ++n, ++g) {
+        const int j = g % NS;
+        const uint32_t buf = lane_addr + 128 * j;
+        wait(&s_full[j], (g / NS) & 1);
+        if (g >= 2) wait(&o_done[g & 1], ((g - 2) >> 1) & 1);  // P V(g-2): keeps o_done within one phase
+        __syncwarp();
+        tc_fence_after();
+        uint32_t sv[128];
+        tmem_ld64x(buf, *reinterpret_cast<uint32_t(*)[64]>(&sv[0]));
+        tmem_ld64x(buf + 64, *reinterpret_cast<uint32_t(*)[64]>(&sv[64]));
+        const int tok0 = (w.j0 + n) * kT;
+        const bool masked = tok0 + kT - 1 > pr || tok0 < first_r;
+        const int lo = first_r - tok0, hi = pr - tok0;  // valid columns [lo, hi]
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (masked) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i < lo || i > hi) sv[i] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int i = 0; i < 128; i += 8) {  // four independent chains of three-input maxima
+          mx[0] = fmax3(mx[0], __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
+          mx[1] = fmax3(mx[1], __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]));
+          mx[2] = fmax3(mx[2], __uint_as_float(sv[i + 4]), __uint_as_float(sv[i + 5]));
+          mx[3] = fmax3(mx[3], __uint_as_float(sv[i + 6]), __uint_as_float(sv[i + 7]));
+        }
+        const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+        const bool grow = m_tile > m_run + kRescaleLog2;
+        if (__any_sync(0xffffffffu, grow)) {
+          const float m_new = grow ? m_tile : m_run;
+          // 0 while the row has seen no unmasked token (O and l are still zero), 1 when unchanged
+          const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - m_new);
+          if (n > 0) {  // rescale O in TMEM once P V(g-1) finished
+            wait(&o_done[(g - 1) & 1], ((g - 1) >> 1) & 1);
+            __syncwarp();
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              float o[32];
+              uint32_t u[32];
+              tmem_ld32(o_addr + 32 * c, o);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * alpha);
+              tmem_st32(o_addr + 32 * c, u);
+            }
+          }
+          l_run *= alpha;
+          m_run = m_new;
+        }
+        const float mu = m_run == -INFINITY ? 0.f : m_run;
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const int kc = 64 * c + i;
+            const bool poly = poly_pair(kc / 2);
+            const float x0 = fmaf(__uint_as_float(sv[kc]), sl2, -mu);
+            const float x1 = fmaf(__uint_as_float(sv[kc + 1]), sl2, -mu);
+            const float e0 = poly ? ex2_poly(x0) : ex2(x0);
+            const float e1 = poly ? ex2_poly(x1) : ex2(x1);
+            sum[(i >> 1) & 3] += e0 + e1;
+            pk[i / 2] = pack_half2(e0, e1);
+          }
+          tmem_st32(buf + 32 * c, pk);
+        }
+        tmem_wait_st();
+        l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+        tc_fence_before();
+        mbar_arrive(&p_full[j]);
+      }
+      // ---- item epilogue: normalise and store this row's outputs, then free O
+      // the last step waited for P V(g-3); now P V(g-2) and P V(g-1)
+      if (g >= 2) wait(&o_done[g & 1], ((g - 2) >> 1) & 1);
+      wait(&o_done[(g - 1) & 1], ((g - 1) >> 1) & 1);
       __syncwarp();
       tc_fence_after();
-      uint32_t sv[128];
-      tmem_ld64x(buf, *reinterpret_cast<uint32_t(*)[64]>(&sv[0]));
-      tmem_ld64x(buf + 64, *reinterpret_cast<uint32_t(*)[64]>(&sv[64]));
-      const int tok0 = (j0 + n) * kT;
-      const bool masked = tok0 + kT - 1 > pr || tok0 < first_r;
-      const int lo = first_r - tok0, hi = pr - tok0;  // valid columns [lo, hi]
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (masked) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const int row = w.row0 + r;
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i < lo || i > hi) sv[i] = __float_as_uint(-INFINITY);
-      }
+      for (int c = 0; c < D / 32; ++c) {
+        float o[32];
+        tmem_ld32(o_addr + 32 * c, o);
+        if (row < p.S) {
+          OUT* dst = static_cast<OUT*>(p.out) + ((static_cast<size_t>(w.b) * p.S + row) * p.Hq + w.h) * D + 32 * c;
+          if constexpr (sizeof(OUT) == 2) {
 #pragma unroll
-      for (int i = 0; i < 128; i += 8) {  // four independent chains of three-input maxima
-        mx[0] = fmax3(mx[0], __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
-        mx[1] = fmax3(mx[1], __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]));
-        mx[2] = fmax3(mx[2], __uint_as_float(sv[i + 4]), __uint_as_float(sv[i + 5]));
-        mx[3] = fmax3(mx[3], __uint_as_float(sv[i + 6]), __uint_as_float(sv[i + 7]));
-      }
-      const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
-      const bool grow = m_tile > m_run + kRescaleLog2;
-      if (__any_sync(0xffffffffu, grow)) {
-        const float m_new = grow ? m_tile : m_run;
-        // 0 while the row has seen no unmasked token (O and l are still zero), 1 when unchanged
-        const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - m_new);
-        if (n > 0) {  // rescale O in TMEM once P V(n-1) finished
-          wait(&o_done[(n - 1) & 1], ((n - 1) >> 1) & 1);
-          __syncwarp();
-          tc_fence_after();
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(dst + i) =
+                  make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv), pack_half2(o[i + 2] * inv, o[i + 3] * inv),
+                             pack_half2(o[i + 4] * inv, o[i + 5] * inv), pack_half2(o[i + 6] * inv, o[i + 7] * inv));
+          } else {
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            float o[32];
-            uint32_t u[32];
-            tmem_ld32(o_addr + 32 * c, o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * alpha);
-            tmem_st32(o_addr + 32 * c, u);
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(dst + i) =
+                  make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
           }
         }
-        l_run *= alpha;
-        m_run = m_new;
       }
-      const float mu = m_run == -INFINITY ? 0.f : m_run;
-      float sum[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const int kc = 64 * c + i;
-          const bool poly = poly_pair(kc / 2);
-          const float x0 = fmaf(__uint_as_float(sv[kc]), sl2, -mu), x1 = fmaf(__uint_as_float(sv[kc + 1]), sl2, -mu);
-          const float e0 = poly ? ex2_poly(x0) : ex2(x0);
-          const float e1 = poly ? ex2_poly(x1) : ex2(x1);
-          sum[(i >> 1) & 3] += e0 + e1;
-          pk[i / 2] = pack_half2(e0, e1);
-        }
-        tmem_st32(buf + 32 * c, pk);
-      }
-      tmem_wait_st();
-      l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
       tc_fence_before();
-      mbar_arrive(&p_full[j]);
-    }
-    // ---- epilogue: normalise and store this row's outputs
-    // the last step waited for P V(N-3); now P V(N-2) and P V(N-1)
-    if (N >= 2) wait(&o_done[N & 1], ((N - 2) >> 1) & 1);
-    wait(&o_done[(N - 1) & 1], ((N - 1) >> 1) & 1);
-    __syncwarp();
-    tc_fence_after();
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    const int row = row0 + r;
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      float o[32];
-      tmem_ld32(o_addr + 32 * c, o);
-      if (row < p.S) {
-        OUT* dst = static_cast<OUT*>(p.out) + ((static_cast<size_t>(b) * p.S + row) * p.Hq + h) * D + 32 * c;
-        if constexpr (sizeof(OUT) == 2) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8)
-            *reinterpret_cast<uint4*>(dst + i) =
-                make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv), pack_half2(o[i + 2] * inv, o[i + 3] * inv),
-                           pack_half2(o[i + 4] * inv, o[i + 5] * inv), pack_half2(o[i + 6] * inv, o[i + 7] * inv));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(dst + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
-        }
-      }
+      mbar_arrive(&o_free[k % C::kNO]);
     }
   }
   tc_fence_before();
@@ -532,7 +615,8 @@ cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32
   p.batch = batch;
   p.scale_log2 = L->attn_scale * kLog2e;
   p.num_m = (seq_len + 127) / 128;
-  const dim3 grid(static_cast<unsigned>(p.num_m * batch * L->Hq));
+  const int items = p.num_m * batch * L->Hq;
+  const dim3 grid(static_cast<unsigned>(items < L->ctx->sm_count ? items : L->ctx->sm_count));
   if (L->D == 64) {
     if (L->io_fp32)
       prefill_tc_kernel<64, float><<<grid, kThreads, PCfg<64>::kSmem, stream>>>(p);
