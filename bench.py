@@ -164,7 +164,8 @@ class Decode1B:
         self.config = {"workload": "decode_1b (config 2): 16 layers x 32q/8kv heads x d64, fp16 KV, 4096 cached + 1 "
                                    "new, theta 5e5", "batch_per_gpu": B, "global_batch": B * world,
                        "parallelism": f"batch-sharded x{world}",
-                       "l2": "inputs (8.6 GB of cache per step per GPU) larger than L2; no flush"}
+                       "l2": f"inputs ({self.bytes_per_step / 1e9:.2f} GB of cache per step per GPU, "
+                             f"{self.bytes_per_launch / 1e6:.0f} MB per layer) larger than L2; no flush"}
         self.scaling = "weak"
 
     def step(self, record=None):
