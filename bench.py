@@ -269,13 +269,14 @@ class LongCtx:
         self.bytes_per_step = L * decode_seq_bytes(T + 1, Hq, Hk, D) / world  # this rank's share
         self.bytes_per_launch = decode_seq_bytes(local, Hq, Hk, D)
         self.tokens_per_step = 1 / world
-        self.launches_per_step = (2 if world == 1 else 3) * L  # decode, merge (+ exchange or combine)
+        # one GPU: decode + merge; p2p: decode + fused merge/exchange; nccl: decode + merge + combine
+        self.launches_per_step = (2 if world == 1 or mode == "p2p" else 3) * L
         if world == 1:
             self.kernel = "decode_fast_kernel<128,half> + decode_merge_kernel (one shard: plain decode)"
             xname = "none"
         elif mode == "p2p":
-            self.kernel = "decode_fast_kernel<128,half> partial + exchange_combine_kernel (NVLink stores + merge)"
-            xname = "peer-memory exchange kernel (NVLink stores, flag wait) + LSE merge"
+            self.kernel = "decode_fast_kernel<128,half> partial + decode_exchange_kernel (segment merge, NVLink exchange, LSE merge)"
+            xname = "fused segment merge + peer-memory exchange (NVLink stores, epoch-word wait) + LSE merge"
         else:
             self.kernel = "decode_fast_kernel<128,half> partial + NCCL all-gather + combine_lse_kernel"
             xname = "NCCL all-gather of (m,l,o) + LSE merge"

@@ -193,6 +193,17 @@ int tla_exchange_buffer(tla_exchange* exchange, void** buffer_out);
 int tla_exchange_connect_buffers(tla_exchange* exchange, void* const* buffers /* [ranks] */);
 int tla_exchange_destroy(tla_exchange* exchange);
 
+/* tla_decode_partial fused with the exchange: this rank's split-KV decode
+ * over its token block, then one kernel that merges each query row's segments,
+ * exchanges the row's triple with every rank of `exchange` and writes the
+ * merged output ([batch][head_count][head_dim], the layer's I/O type, times
+ * sigmoid(gate) when gate is given). partial: caller scratch of
+ * batch * head_count * (head_dim + 2) floats. Every rank calls it once per
+ * step. No counterpart in the reference. */
+int tla_decode_exchange(tla_layer* layer, tla_exchange* exchange, const void* qkv, const int32_t* positions,
+                        int32_t slot_offset, int32_t local_tokens, int32_t append, float* partial, const void* gate,
+                        void* out, int32_t batch, void* stream);
+
 /* reset() (TSLAttention.ts:434-441): zero the cache. A borrowing layer is a no-op. */
 int tla_cache_reset(tla_layer* layer, void* stream);
 

@@ -48,6 +48,44 @@ def test_exchange_one_rank_matches_combine_lse(pkg, cuda):
         ex.close()
 
 
+@pytest.mark.parametrize("D,T", [(128, 20000), (64, 3000)])
+def test_decode_exchange_one_rank_equals_decode(pkg, cuda, D, T):
+    """tla_decode_exchange with a single rank: the split-KV kernel, the fused
+    segment merge and the exchange path must reproduce the plain decode."""
+    from three_llm_b200 import _abi, sharding
+    from three_llm_b200._abi import check, lib
+    from three_llm_b200.attention import _ptr, _stream
+
+    Hq, Hk = 32, 8
+    g = torch.Generator(device=cuda)
+    g.manual_seed(9)
+    opts = {"headDim": D, "kvHeadCount": Hk, "ropeTheta": 5e5, "dtype": torch.float16}
+    a = pkg.CUDAAttention(None, Hq * D, Hq, T + 1, opts)
+    b = pkg.CUDAAttention(None, Hq * D, Hq, T + 1, opts)
+    kv = torch.randn(T + 1, Hk * D, generator=g, device=cuda).cpu().numpy()
+    vv = torch.randn(T + 1, Hk * D, generator=g, device=cuda).cpu().numpy()
+    for layer in (a, b):
+        layer.write_cache(0, 0, kv[:T], vv[:T])
+    qkv = torch.randn(1, (Hq + 2 * Hk) * D, generator=g, device=cuda).half()
+    pos = torch.tensor([T], dtype=torch.int32, device=cuda)
+    exp = a.decode(qkv, pos)
+    ex = sharding.PeerExchange(0, 1, Hq * (D + 2) * 4, cuda.index or 0, group=False, context=b.context)
+    try:
+        ex.connect_buffers([ex.buffer()])
+        partial = torch.empty(1, Hq, D + 2, device=cuda)
+        out = torch.empty(1, Hq * D, dtype=torch.float16, device=cuda)
+        for _ in range(2):  # the new token is rewritten in place: both calls see the same inputs
+            check(lib().tla_decode_exchange(b.handle, ex.handle, _ptr(qkv), _ptr(pos), 0, T + 1, 1, _ptr(partial),
+                                            None, _ptr(out), 1, _stream(None)), "decode_exchange")
+        torch.cuda.synchronize()
+        assert b.context.error() == 0
+        torch.testing.assert_close(out.float(), exp.float(), rtol=1e-2, atol=2e-3)
+    finally:
+        ex.close()
+        a.close()
+        b.close()
+
+
 def test_exchange_missing_peer_times_out(pkg, cuda):
     """Rank 1 never runs: rank 0's wait must end with TLA_ERR_TIMEOUT, not hang."""
     from three_llm_b200 import _abi, sharding

@@ -31,7 +31,7 @@ EXPORTS = [
     "tla_layer_share_cache", "tla_layer_destroy", "tla_layer_cache_view", "tla_decode", "tla_prefill",
     "tla_decode_partial", "tla_combine_lse", "tla_cache_reset", "tla_cache_read", "tla_cache_write",
     "tla_decode_noalloc", "tla_exchange_create", "tla_exchange_connect", "tla_exchange_combine",
-    "tla_exchange_buffer", "tla_exchange_connect_buffers", "tla_exchange_destroy",
+    "tla_exchange_buffer", "tla_exchange_connect_buffers", "tla_exchange_destroy", "tla_decode_exchange",
 ]
 
 
@@ -122,6 +122,7 @@ def lib():
         L.tla_exchange_buffer.argtypes = [P, ctypes.POINTER(P)]
         L.tla_exchange_connect_buffers.argtypes = [P, P]
         L.tla_exchange_destroy.argtypes = [P]
+        L.tla_decode_exchange.argtypes = [P, P, P, P, i32, i32, i32, P, P, P, i32, P]
         L.tla_decode_noalloc.argtypes = [ctypes.POINTER(AttnConfig), P, P, P, P, P, P, P, P, P, i32, P]
         for name in EXPORTS:
             if name != "tla_status_string":

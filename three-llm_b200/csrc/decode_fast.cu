@@ -26,6 +26,7 @@
 
 #include <mutex>
 
+#include "exchange.cuh"
 #include "tla_device.cuh"
 #include "tla_internal.h"
 
@@ -789,12 +790,171 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const __gri
   }
 }
 
+// Sequence-shard decode fused with the peer exchange: one 4-warp block per
+// SM walks query rows (b, h). For each row it merges this rank's split-KV
+// segments exactly like decode_merge_kernel (or takes the triple the decode
+// kernel wrote when one CTA held the whole pair), stores the row's triple
+// into every rank's exchange buffer, and after all its rows are out, gathers
+// every rank's triple of each row and writes the log-sum-exp merge.
+template <int D, typename IO>
+__global__ void __launch_bounds__(kMergeThreads) decode_exchange_kernel(const __grid_constant__ DecodeParams p,
+                                                                        int grid, ExchangeDev x) {
+  constexpr int kWarps = kMergeThreads / 32;
+  constexpr int kPer = D / 32;
+  constexpr int W = D + 2;
+  __shared__ long long prefix[kMaxBatch + 1];
+  __shared__ int seg_slot[kMaxGrid];
+  __shared__ float seg_w[kMaxGrid];
+  __shared__ float seg_l[kMaxGrid];
+  __shared__ float red[2][kWarps];
+  __shared__ float rows_s[kWarps][D];
+  __shared__ __align__(16) float trip[W];
+  __shared__ __align__(16) float vals[kXchMaxRanks * W];
+  __shared__ int epoch_s;
+  __shared__ float wts[kXchMaxRanks];
+  __shared__ float ls;
+  const LayerArgs& a = p.a;
+  const int G = a.G, Hk = a.Hk, Hq = a.Hq;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int bb = tid; bb < p.batch; bb += kMergeThreads) {
+    const int pos = p.positions[bb];
+    int lo, hi;
+    seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
+    const bool ok = pos >= 0 && (!p.append || (pos - p.slot_offset >= 0 && pos - p.slot_offset < a.max_tokens &&
+                                                pos - p.slot_offset == hi));
+    prefix[bb + 1] = (ok && hi >= lo) ? static_cast<long long>((hi - lo + kTile) / kTile) * Hk : 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    long long acc = 0;
+    prefix[0] = 0;
+    for (int bb = 1; bb <= p.batch; ++bb) {
+      acc += prefix[bb];
+      prefix[bb] = acc;
+    }
+  }
+  const unsigned epoch = xch_epoch(x, &epoch_s);  // syncs the block
+  const long long total = prefix[p.batch];
+  const int rows = p.batch * Hq;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int b = row / Hq, h = row - b * Hq, kvh = h / G, r = h - kvh * G;
+    const int tiles = static_cast<int>((prefix[b + 1] - prefix[b]) / Hk);
+    const long long pb = prefix[b] + static_cast<long long>(kvh) * tiles;
+    const int c0 = tiles ? cta_of(pb, total, grid) : 0, c1 = tiles ? cta_of(pb + tiles - 1, total, grid) : 0;
+    if (tiles == 0 || c0 == c1) {  // written by the decode kernel (empty pair: m = -inf)
+      for (int e = tid; e < W; e += kMergeThreads) trip[e] = __ldcg(p.partial_out + static_cast<size_t>(row) * W + e);
+    } else {
+      const int S = c1 - c0 + 1;
+      float m = -INFINITY;
+      for (int k = tid; k < S; k += kMergeThreads) {
+        const int c = c0 + k;
+        const long long cb = cta_begin(c, total, grid);
+        const int sl = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
+        seg_slot[k] = sl;
+        float mk = -INFINITY, lk = 0.f;
+        if (sl >= 0) {
+          const float* sp = p.scratch + (static_cast<size_t>(sl) * G + r) * W;
+          mk = __ldcg(sp);
+          lk = __ldcg(sp + 1);
+        }
+        seg_w[k] = mk;
+        seg_l[k] = lk;
+        m = fmaxf(m, mk);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) red[0][warp] = m;
+      __syncthreads();
+      float M = red[0][0];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) M = fmaxf(M, red[0][w]);
+      float l = 0.f;
+      for (int k = tid; k < S; k += kMergeThreads) {
+        const float w = (seg_slot[k] < 0 || M == -INFINITY) ? 0.f : ex2(seg_w[k] - M);
+        seg_w[k] = w;
+        l += seg_l[k] * w;
+      }
+      l = warp_sum(l);
+      if (lane == 0) red[1][warp] = l;
+      __syncthreads();
+      const float2* col = reinterpret_cast<const float2*>(p.scratch + static_cast<size_t>(r) * W + 2) + lane;
+      const size_t slot_stride2 = static_cast<size_t>(G) * W / 2;
+      float2 acc[kPer / 2];
+#pragma unroll
+      for (int j = 0; j < kPer / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+      int k = warp;
+      for (; k + 7 * kWarps < S; k += 8 * kWarps) {  // eight segments' loads in flight
+        float2 v[8][kPer / 2];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int sl = seg_slot[k + u * kWarps];
+#pragma unroll
+          for (int j = 0; j < kPer / 2; ++j)
+            v[u][j] = sl >= 0 ? __ldcg(col + static_cast<size_t>(sl) * slot_stride2 + j * 32) : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float w = seg_w[k + u * kWarps];
+#pragma unroll
+          for (int j = 0; j < kPer / 2; ++j) {
+            acc[j].x += v[u][j].x * w;
+            acc[j].y += v[u][j].y * w;
+          }
+        }
+      }
+      for (; k < S; k += kWarps) {
+        const int sl = seg_slot[k];
+        if (sl < 0) continue;
+        const float w = seg_w[k];
+#pragma unroll
+        for (int j = 0; j < kPer / 2; ++j) {
+          const float2 v = __ldcg(col + static_cast<size_t>(sl) * slot_stride2 + j * 32);
+          acc[j].x += v.x * w;
+          acc[j].y += v.y * w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kPer / 2; ++j) {
+        rows_s[warp][2 * (lane + 32 * j)] = acc[j].x;
+        rows_s[warp][2 * (lane + 32 * j) + 1] = acc[j].y;
+      }
+      __syncthreads();
+      for (int d = tid; d < D; d += kMergeThreads) {
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) o += rows_s[w][d];
+        trip[2 + d] = o;
+      }
+      if (tid == 0) {
+        trip[0] = M;
+        trip[1] = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+      }
+    }
+    __syncthreads();
+    xch_push_row(x, epoch, row, trip, W);
+    __syncthreads();  // trip and the segment tables are reused by the next row
+  }
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    xch_gather_row(x, epoch, row, W, vals, a.error);
+    xch_merge_row<IO>(vals, x.ranks, D, p.gate ? static_cast<const IO*>(p.gate) + static_cast<size_t>(row) * D : nullptr,
+                      static_cast<IO*>(p.out) + static_cast<size_t>(row) * D, wts, &ls);
+  }
+  xch_finish(x, epoch);
+}
+
 template <int D, typename IO, bool TWO>
-cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, cudaStream_t stream) {
+cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, const ExchangeDev* x, cudaStream_t stream) {
   const SmemLayout s = smem_layout<D>(L->G, p.batch);
   decode_fast_kernel<D, IO, TWO><<<L->decode_grid, kThreads, s.total, stream>>>(p);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess || !p.defer_merge) return e;
+  if (e != cudaSuccess) return e;
+  if (x != nullptr) {
+    const int rows = p.batch * L->Hq;
+    const int grid = rows < L->ctx->sm_count ? rows : L->ctx->sm_count;
+    decode_exchange_kernel<D, IO><<<grid, kMergeThreads, 0, stream>>>(p, L->decode_grid, *x);
+    return cudaGetLastError();
+  }
+  if (!p.defer_merge) return e;
   decode_merge_kernel<D, IO><<<p.batch * L->Hk * L->G, kMergeThreads, 0, stream>>>(p, L->decode_grid);
   return cudaGetLastError();
 }
@@ -817,10 +977,11 @@ cudaError_t dispatch_configure(tla_layer* L, int* blocks) {
 }
 
 template <int D>
-cudaError_t dispatch_launch(const tla_layer* L, const DecodeParams& p, cudaStream_t stream) {
+cudaError_t dispatch_launch(const tla_layer* L, const DecodeParams& p, const ExchangeDev* x, cudaStream_t stream) {
   const bool two = L->G > 8;
-  if (L->io_fp32) return two ? launch_t<D, float, true>(L, p, stream) : launch_t<D, float, false>(L, p, stream);
-  return two ? launch_t<D, __half, true>(L, p, stream) : launch_t<D, __half, false>(L, p, stream);
+  if (L->io_fp32)
+    return two ? launch_t<D, float, true>(L, p, x, stream) : launch_t<D, float, false>(L, p, x, stream);
+  return two ? launch_t<D, __half, true>(L, p, x, stream) : launch_t<D, __half, false>(L, p, x, stream);
 }
 
 CUresult make_cache_map(const tla_layer* L, void* base, CUtensorMap* map) {
@@ -863,9 +1024,9 @@ size_t decode_fast_scratch_floats(const tla_layer* L) {
   return static_cast<size_t>(L->decode_grid) * 2 * L->G * (L->D + 2);
 }
 
-cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_t* positions, const void* gate,
-                               void* out, float* partial, int batch, int slot_offset, int local_tokens, int append,
-                               cudaStream_t stream) {
+namespace {
+DecodeParams decode_params(const tla_layer* L, const void* qkv, const int32_t* positions, const void* gate, void* out,
+                           float* partial, int batch, int slot_offset, int local_tokens, int append) {
   DecodeParams p;
   p.tmap_k = L->tmap_k;
   p.tmap_v = L->tmap_v;
@@ -884,7 +1045,23 @@ cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_
   // Few, long sequences split each (sequence, kv head) over many CTAs: merge
   // those in a separate, fully parallel kernel instead of in the last CTA.
   p.defer_merge = L->decode_grid > 4 * batch * L->Hk ? 1 : 0;
-  return L->D == 64 ? dispatch_launch<64>(L, p, stream) : dispatch_launch<128>(L, p, stream);
+  return p;
+}
+}  // namespace
+
+cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_t* positions, const void* gate,
+                               void* out, float* partial, int batch, int slot_offset, int local_tokens, int append,
+                               cudaStream_t stream) {
+  const DecodeParams p = decode_params(L, qkv, positions, gate, out, partial, batch, slot_offset, local_tokens, append);
+  return L->D == 64 ? dispatch_launch<64>(L, p, nullptr, stream) : dispatch_launch<128>(L, p, nullptr, stream);
+}
+
+cudaError_t launch_decode_exchange(const tla_layer* L, const ExchangeDev& x, const void* qkv,
+                                   const int32_t* positions, const void* gate, void* out, float* partial, int batch,
+                                   int slot_offset, int local_tokens, int append, cudaStream_t stream) {
+  DecodeParams p = decode_params(L, qkv, positions, gate, out, partial, batch, slot_offset, local_tokens, append);
+  p.defer_merge = 1;  // the segments are merged by decode_exchange_kernel
+  return L->D == 64 ? dispatch_launch<64>(L, p, &x, stream) : dispatch_launch<128>(L, p, &x, stream);
 }
 
 }  // namespace tla

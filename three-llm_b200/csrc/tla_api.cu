@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "tla_device.cuh"
+#include "exchange.cuh"
 #include "tla_internal.h"
 
 namespace tla {
@@ -398,6 +399,29 @@ int tla_decode_partial(tla_layer* L, const void* qkv, const int32_t* positions, 
   if (rc != TLA_OK) return rc;
   return from_cuda(tla::launch_attend_generic(L, qs, positions, batch, 1, slot_offset, local_tokens, nullptr, nullptr,
                                               partial, st));
+}
+
+int tla_decode_exchange(tla_layer* L, tla_exchange* ex, const void* qkv, const int32_t* positions, int32_t slot_offset,
+                        int32_t local_tokens, int32_t append, float* partial, const void* gate, void* out, int32_t batch,
+                        void* stream) {
+  if (!valid_layer(L) || !ex || !qkv || !positions || !partial || !out || batch < 0 || batch > L->max_batch ||
+      slot_offset < 0 || local_tokens < 0 || local_tokens > L->max_tokens)
+    return TLA_ERR_INVALID_ARG;
+  if (append && L->borrowed) return TLA_ERR_SHARED;
+  if (batch == 0) return TLA_OK;
+  const size_t need = static_cast<size_t>(batch) * L->Hq * (L->D + 2) * sizeof(float);
+  if (need > tla::exchange_slot_bytes(ex)) return TLA_ERR_INVALID_ARG;
+  if (!L->fast_decode) {  // generic shapes: the partial kernel, then the exchange kernel
+    int rc = tla_decode_partial(L, qkv, positions, slot_offset, local_tokens, append, partial, batch, stream);
+    if (rc != TLA_OK) return rc;
+    return tla_exchange_combine(ex, partial, batch, L->Hq, L->D, gate, out, L->io_fp32 ? TLA_FLAG_IO_FP32 : 0u,
+                                stream);
+  }
+  tla::ExchangeDev x;
+  if (!tla::exchange_device_view(ex, &x)) return TLA_ERR_INVALID_ARG;
+  DeviceGuard g(L->ctx->device);
+  return from_cuda(tla::launch_decode_exchange(L, x, qkv, positions, gate, out, partial, batch, slot_offset,
+                                               local_tokens, append ? 1 : 0, static_cast<cudaStream_t>(stream)));
 }
 
 int tla_combine_lse(const float* partials, int32_t ranks, int32_t batch, int32_t head_count, int32_t head_dim,

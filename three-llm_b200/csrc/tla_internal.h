@@ -89,6 +89,17 @@ cudaError_t launch_rope_append_half_q(const tla_layer* L, const void* qkv, const
 cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_t* positions, const void* gate,
                                void* out, float* partial, int batch, int slot_offset, int local_tokens, int append,
                                cudaStream_t stream);
+// Peer exchange (exchange.cu / exchange.cuh): device view of a connected exchange.
+struct ExchangeDev;
+bool exchange_device_view(const tla_exchange* ex, ExchangeDev* out);
+size_t exchange_slot_bytes(const tla_exchange* ex);
+// Sequence-shard decode fused with the exchange: the split-KV kernel writes
+// this rank's segments (partial: [B][Hq][D+2] for pairs held by one CTA), then
+// one kernel merges each query row's segments, exchanges the row's triple with
+// every rank and writes the merged output.
+cudaError_t launch_decode_exchange(const tla_layer* L, const ExchangeDev& x, const void* qkv,
+                                   const int32_t* positions, const void* gate, void* out, float* partial, int batch,
+                                   int slot_offset, int local_tokens, int append, cudaStream_t stream);
 cudaError_t decode_fast_configure(tla_layer* L);
 cudaError_t launch_combine_lse(const float* partials, int ranks, int batch, int Hq, int D, const void* gate,
                                void* out, bool io_fp32, cudaStream_t stream);

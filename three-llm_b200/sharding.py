@@ -125,12 +125,13 @@ class PeerExchange:
 class SequenceShardedDecode:
     """One layer of long-context decode sharded by token blocks.
 
-    step(): tla_decode_partial on this rank's block, then the (m, l, o)
-    triples of all ranks are merged: exchange="nccl" all-gathers them over the
-    process group and runs tla_combine_lse; exchange="p2p" hands them to a
-    PeerExchange (one kernel: NVLink stores, bounded flag wait, merge). Every
-    rank ends with the full output [B, Hq*D] (fp16). All ranks take the same
-    steps in the same order.
+    step(): exchange="nccl" runs tla_decode_partial on this rank's block,
+    all-gathers the (m, l, o) triples over the process group and merges them
+    with tla_combine_lse; exchange="p2p" runs tla_decode_exchange (the
+    split-KV kernel, then one kernel that merges each row's segments, stores
+    the row's triple into every rank's PeerExchange buffer over NVLink, waits
+    for the peers' triples and merges). Every rank ends with the full output
+    [B, Hq*D] (fp16). All ranks take the same steps in the same order.
     """
 
     def __init__(self, head_count, kv_head_count, head_dim, total_tokens, rank, world, options=None, batch=1,
@@ -162,10 +163,14 @@ class SequenceShardedDecode:
             return self.layer.decode(qkv.view(self.B, -1), positions, out=self.out, stream=stream)
         s = self.shard
         local = s.tokens + (1 if s.owns_next else 0)
+        if self.exchange is not None:  # split-KV decode + segment merge + NVLink exchange + merge: two kernels
+            self.layer._check_io(qkv, "qkv")
+            check(lib().tla_decode_exchange(self.layer.handle, self.exchange.handle, _ptr(qkv), _ptr(positions),
+                                            s.slot_offset, local, 1 if s.owns_next else 0, _ptr(self.partial),
+                                            None, _ptr(self.out), self.B, _stream(stream)), "tla_decode_exchange")
+            return self.out
         self.layer.decode_partial(qkv, positions, s.slot_offset, local, s.owns_next, partial=self.partial,
                                   stream=stream)
-        if self.exchange is not None:
-            return self.exchange.combine(self.partial, self.out, stream=stream)
         if self.world > 1:
             torch.distributed.all_gather_into_tensor(self.gathered.view(-1), self.partial.view(-1), group=self.group)
             parts = self.gathered
