@@ -165,8 +165,10 @@ class Decode1B:
                                    "new, theta 5e5", "batch_per_gpu": B, "global_batch": B * world,
                        "parallelism": f"batch-sharded x{world}",
                        "l2": f"inputs ({self.bytes_per_step / 1e9:.2f} GB of cache per step per GPU, "
-                             f"{self.bytes_per_launch / 1e6:.0f} MB per layer) larger than L2; no flush"}
+                             f"{self.bytes_per_launch / 1e6:.0f} MB per layer) larger than L2; no flush",
+                       "launch": "step captured as one CUDA graph (per-layer kernel times from an eager pass)"}
         self.scaling = "weak"
+        self.use_graph = True
 
     def step(self, record=None):
         for i, layer in enumerate(self.layers):
@@ -235,8 +237,10 @@ class Ragged8B(Decode1B):
         self.config = {"workload": "ragged_8b (config 4): 32 layers x 32q/8kv heads x d128, fp16 KV, batch 64, "
                                    "context U[512, 8192] (seed 0), theta 5e5", "global_batch": B,
                        "parallelism": f"kv-head groups x{world} ({hk} kv / {hq} q heads per GPU)",
-                       "l2": "inputs larger than L2; no flush"}
+                       "l2": "inputs larger than L2; no flush",
+                       "launch": "step captured as one CUDA graph (per-layer kernel times from an eager pass)"}
         self.scaling = "strong"
+        self.use_graph = True
 
 
 class LongCtx:
@@ -567,7 +571,7 @@ def main():
                                            "per call", "tflops": round(pre["tflops"], 2), "ms": round(pre["ms"], 5),
                                "causal_gflop": round(pre["flops"] / 1e9, 3), "frac": round(pre["tflops"] / tc, 4),
                                "peak_tflops": tc, "peak_source": src,
-                               "kernels": "rope_append_warp_kernel + prefill_tc_kernel<64,half>"}
+                               "kernels": "rope_rows_kernel<64> + prefill_tc_kernel<64,half> (persistent)"}
         if not args.no_cpu_baseline:
             gb, dt, desc = cpu_decode_sample(1, args.workload, batch=4 if args.workload == "decode_1b" else 1)
             line["cpu_baseline"] = {"value": round(gb, 4), "unit": "GB/s", "cores": 1, "kind": "port",
