@@ -44,6 +44,14 @@ METRIC = "decode attn GB/s (%HBM) + tok/s @1/2/4/8 B200; prefill attn TFLOP/s"
 DECODE_1B = dict(Hq=32, Hk=8, D=64, T=4096, layers=16, theta=500000.0, batch=64)
 RAGGED_8B = dict(Hq=32, Hk=8, D=128, layers=32, theta=500000.0, batch=64, lo=512, hi=8192)
 LONG_CTX = dict(Hq=32, Hk=8, D=128, T=131072, layers=32, theta=500000.0, batch=1)
+WORKLOAD_LABELS = {
+    "decode_1b": "decode_1b (config 2): 16 layers x 32q/8kv heads x d64, fp16 KV, 4096 cached + 1 new, theta 5e5",
+    "ragged_8b": "ragged_8b (config 4): 32 layers x 32q/8kv heads x d128, fp16 KV, batch 64, context U[512, 8192] "
+                 "(seed 0), theta 5e5",
+    "long_ctx": "long_ctx (config 5): 32 layers x 32q/8kv heads x d128, one sequence, 131072 cached tokens + 1 new, "
+                "fp16 KV, theta 5e5",
+    "prefill_05b": "prefill_05b (config 3)",
+}
 PREFILL_05B = dict(Hq=14, Hk=2, D=64, S=2048, B=4, T=4096, theta=1e6)
 
 
@@ -161,8 +169,7 @@ class Decode1B:
         self.tokens_per_step = B
         self.launches_per_step = L
         self.kernel = "decode_fast_kernel<64,half>"
-        self.config = {"workload": "decode_1b (config 2): 16 layers x 32q/8kv heads x d64, fp16 KV, 4096 cached + 1 "
-                                   "new, theta 5e5", "batch_per_gpu": B, "global_batch": B * world,
+        self.config = {"workload": WORKLOAD_LABELS["decode_1b"], "batch_per_gpu": B, "global_batch": B * world,
                        "parallelism": f"batch-sharded x{world}",
                        "l2": f"inputs ({self.bytes_per_step / 1e9:.2f} GB of cache per step per GPU, "
                              f"{self.bytes_per_launch / 1e6:.0f} MB per layer) larger than L2; no flush",
@@ -234,8 +241,7 @@ class Ragged8B(Decode1B):
         deferred = 2 * sms > 4 * B * hk
         self.launches_per_step = L * (2 if deferred else 1)
         self.kernel = "decode_fast_kernel<128,half>" + (" + decode_merge_kernel" if deferred else "")
-        self.config = {"workload": "ragged_8b (config 4): 32 layers x 32q/8kv heads x d128, fp16 KV, batch 64, "
-                                   "context U[512, 8192] (seed 0), theta 5e5", "global_batch": B,
+        self.config = {"workload": WORKLOAD_LABELS["ragged_8b"], "global_batch": B,
                        "parallelism": f"kv-head groups x{world} ({hk} kv / {hq} q heads per GPU)",
                        "l2": "inputs larger than L2; no flush",
                        "launch": "step captured as one CUDA graph (per-layer kernel times from an eager pass)"}
@@ -284,8 +290,7 @@ class LongCtx:
         else:
             self.kernel = "decode_fast_kernel<128,half> partial + NCCL all-gather + combine_lse_kernel"
             xname = "NCCL all-gather of (m,l,o) + LSE merge"
-        self.config = {"workload": "long_ctx (config 5): 32 layers x 32q/8kv heads x d128, one sequence, 131072 "
-                                   "cached tokens + 1 new, fp16 KV, theta 5e5", "global_batch": 1,
+        self.config = {"workload": WORKLOAD_LABELS["long_ctx"], "global_batch": 1,
                        "parallelism": f"sequence blocks x{world}, {xname} per layer",
                        "l2": "inputs larger than L2; no flush"}
         self.scaling = "strong"
@@ -480,8 +485,8 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "sample": desc},
+        "scaling": "weak" if args.workload == "decode_1b" else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD_LABELS[args.workload], "sample": desc},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
