@@ -249,8 +249,49 @@ class Ragged8B(Decode1B):
         self.use_graph = True
 
 
+class LongCtxHeads(Decode1B):
+    """Config 5 sharded by KV-head group: rank r holds kv heads [r Hk/N, (r+1) Hk/N)
+    of the one 131072-token sequence and their query groups, so its layer is a
+    smaller layer, there is no exchange, and the output stays head-sharded for
+    a tensor-parallel output projection (as config 4)."""
+
+    def __init__(self, pkg, torch, device, rank, world, args):
+        from three_llm_b200 import sharding
+
+        w = LONG_CTX
+        self.torch = torch
+        L, T, Hq, Hk, D = w["layers"], w["T"], w["Hq"], w["Hk"], w["D"]
+        sh = sharding.head_shard(Hq, Hk, world, rank)
+        hq, hk = sh.q_count, sh.kv_count
+        gen = torch.Generator(device=device)
+        gen.manual_seed(5 + rank)
+        self.layers = []
+        for _ in range(L):
+            layer = pkg.CUDAAttention(None, hq * D, hq, T + 1, {"headDim": D, "kvHeadCount": hk,
+                                                                "ropeTheta": w["theta"], "dtype": torch.float16})
+            fill_cache_random(layer, gen, torch)
+            self.layers.append(layer)
+        self.qkv = torch.randn(L, 1, (hq + 2 * hk) * D, generator=gen, device=device).half()
+        self.pos = torch.full((1,), T, dtype=torch.int32, device=device)
+        self.outs = torch.empty(L, 1, hq * D, dtype=torch.float16, device=device)
+        self.bytes_per_step = L * decode_seq_bytes(T + 1, hq, hk, D)
+        self.bytes_per_launch = decode_seq_bytes(T + 1, hq, hk, D)
+        self.tokens_per_step = 1 / world  # the ranks together produce the sequence's next token
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        deferred = 2 * sms > 4 * hk
+        self.launches_per_step = L * (2 if deferred else 1)
+        self.kernel = "decode_fast_kernel<128,half>" + (" + decode_merge_kernel" if deferred else "")
+        self.config = {"workload": WORKLOAD_LABELS["long_ctx"], "global_batch": 1,
+                       "parallelism": f"kv-head groups x{world} ({hk} kv / {hq} q heads per GPU, no exchange)",
+                       "l2": "inputs larger than L2; no flush",
+                       "launch": "32-layer step captured as one CUDA graph (per-layer kernel times from an eager pass)"}
+        self.scaling = "strong"
+        self.use_graph = True
+
+
 class LongCtx:
-    """Config 5, sharded by token blocks with an NCCL all-gather + LSE merge per layer."""
+    """Config 5 on one GPU, or sharded by token blocks: each rank decodes its block and the
+    per-head (m, l, o) triples meet in the fused peer exchange (or an NCCL all-gather)."""
 
     def __init__(self, pkg, torch, device, rank, world, args):
         from three_llm_b200 import sharding
@@ -363,6 +404,14 @@ def run_prefill(pkg, torch, device, args):
 
 
 WORKLOADS = {"decode_1b": Decode1B, "ragged_8b": Ragged8B, "long_ctx": LongCtx}
+
+
+def make_workload(name, pkg, torch, device, rank, world, args):
+    # long_ctx: KV-head groups while they divide the ranks (no exchange per
+    # layer), else token blocks with the peer exchange (or NCCL)
+    if name == "long_ctx" and args.long_parallel != "sequence" and LONG_CTX["Hk"] % world == 0 and world > 1:
+        return LongCtxHeads(pkg, torch, device, rank, world, args)
+    return WORKLOADS[name](pkg, torch, device, rank, world, args)
 
 
 def timed(torch, wl, args, world, device):
@@ -507,6 +556,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="long_ctx merge of the sequence shards across GPUs")
+    ap.add_argument("--long-parallel", default="heads", choices=["heads", "sequence"],
+                    help="long_ctx on several GPUs: KV-head groups (when they divide the GPUs) or token blocks")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -543,7 +594,7 @@ def main():
             torch.distributed.destroy_process_group()
         return
 
-    wl = WORKLOADS[args.workload](pkg, torch, device, rank, world, args)
+    wl = make_workload(args.workload, pkg, torch, device, rank, world, args)
     elapsed, e2e_ms, per_launch, clocks = timed(torch, wl, args, world, device)
     pre = run_prefill(pkg, torch, device, args) if (args.workload == "decode_1b" and not args.no_prefill) else None
     t = torch.tensor([elapsed, e2e_ms], dtype=torch.float64, device=device)
