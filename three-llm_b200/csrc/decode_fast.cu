@@ -640,19 +640,20 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
 }
 
 // Deferred merge for pairs split across many CTAs (few, long sequences): one
-// block of 4 warps per (pair, query row). The segment table (scratch slot and
+// block of NT / 32 warps per (pair, query row); 16 warps when a pair spans 64
+// or more CTAs (one long sequence per kv head: up to the whole grid). The segment table (scratch slot and
 // weight of every contributing CTA) is built once in shared memory; then warp
-// w sums segments w, w + 4, ... with each lane holding D / 32 output columns,
-// eight segments' loads in flight at a time, and the four partial rows are
+// w sums segments w, w + NT / 32, ... with each lane holding D / 32 output columns,
+// eight segments' loads in flight at a time, and the warps' partial rows are
 // added through shared memory. Pairs covered by a single CTA were written by
 // the decode kernel and are skipped.
 constexpr int kMaxGrid = 16 * 128;  // the host keeps decode_grid <= 16 * D
 constexpr int kMergeThreads = 128;
 
-template <int D, typename IO>
-__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const __grid_constant__ DecodeParams p,
+template <int D, typename IO, int NT>
+__global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant__ DecodeParams p,
                                                                      int grid) {
-  constexpr int kWarps = kMergeThreads / 32;
+  constexpr int kWarps = NT / 32;
   constexpr int kPer = D / 32;  // output columns per lane (float2 loads)
   __shared__ long long prefix[kMaxBatch + 1];
   __shared__ int seg_slot[kMaxGrid];   // scratch slot of segment k, -1 if none
@@ -666,7 +667,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const __gri
   const int b = pair / Hk, kvh = pair - b * Hk;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // the decode kernel's partition, recomputed: tile counts in parallel, then a serial scan
-  for (int bb = tid; bb < p.batch; bb += kMergeThreads) {
+  for (int bb = tid; bb < p.batch; bb += NT) {
     const int pos = p.positions[bb];
     int lo, hi;
     seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
@@ -693,7 +694,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const __gri
   if (c0 == c1) return;  // one CTA held the whole pair
   const int S = c1 - c0 + 1;
   float m = -INFINITY;
-  for (int k = tid; k < S; k += kMergeThreads) {
+  for (int k = tid; k < S; k += NT) {
     const int c = c0 + k;
     const long long cb = cta_begin(c, total, grid);
     const int sl = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
@@ -716,7 +717,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const __gri
 #pragma unroll
   for (int w = 1; w < kWarps; ++w) M = fmaxf(M, red[0][w]);
   float l = 0.f;
-  for (int k = tid; k < S; k += kMergeThreads) {
+  for (int k = tid; k < S; k += NT) {
     const float w = (seg_slot[k] < 0 || M == -INFINITY) ? 0.f : ex2(seg_w[k] - M);
     seg_w[k] = w;
     l += seg_l[k] * w;
@@ -771,7 +772,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const __gri
   }
   __syncthreads();
   const size_t hrow = static_cast<size_t>(b) * a.Hq + kvh * G + r;
-  for (int d = tid; d < D; d += kMergeThreads) {
+  for (int d = tid; d < D; d += NT) {
     float o = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) o += rows_s[w][d];
@@ -955,7 +956,11 @@ cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, const ExchangeDe
     return cudaGetLastError();
   }
   if (!p.defer_merge) return e;
-  decode_merge_kernel<D, IO><<<p.batch * L->Hk * L->G, kMergeThreads, 0, stream>>>(p, L->decode_grid);
+  const int pairs = p.batch * L->Hk;
+  if (L->decode_grid >= 64 * pairs)
+    decode_merge_kernel<D, IO, 512><<<pairs * L->G, 512, 0, stream>>>(p, L->decode_grid);
+  else
+    decode_merge_kernel<D, IO, kMergeThreads><<<pairs * L->G, kMergeThreads, 0, stream>>>(p, L->decode_grid);
   return cudaGetLastError();
 }
 
