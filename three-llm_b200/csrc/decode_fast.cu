@@ -49,6 +49,22 @@ constexpr int kMaxBatch = 1024;      // prefix table in shared memory
 #define TLA_DECODE_STAGES_D128 2
 #endif
 
+#ifdef TLA_DECODE_TRACE
+// Optional per-CTA timeline (builds with -DTLA_DECODE_TRACE only): globaltimer
+// at [cta][0] entry, [1] partition done, [2] first tile landed (consumer warp
+// 0), [3] last tile consumed, [4] exit, [5] first TMA issued, [6] first
+// segment's query set-up done; read with tla_debug_decode_trace.
+__device__ unsigned long long g_decode_trace[2048][10];
+#define DTRACE(ev) \
+  do { \
+    if (blockIdx.x < 2048) g_decode_trace[blockIdx.x][(ev)] = globaltimer(); \
+  } while (0)
+#else
+#define DTRACE(ev) \
+  do { \
+  } while (0)
+#endif
+
 template <int D>
 struct Cfg {
   static constexpr int kStages = D == 64 ? TLA_DECODE_STAGES_D64 : TLA_DECODE_STAGES_D128;
@@ -147,6 +163,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
   volatile int* flags = reinterpret_cast<volatile int*>(smem + L.flags);  // [0] abort, [1] last-CTA ticket
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int grid = gridDim.x, cta = blockIdx.x;
+  if (tid == 0) DTRACE(0);
 
   // ---- partition: tiles per sequence, prefix over (sequence, kv head) pairs
   for (int b = tid; b < p.batch; b += kThreads) {
@@ -204,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       }
     }
   }
+  if (tid == 0) DTRACE(1);
   if (total == 0) return;
   const long long tb = cta_begin(cta, total, grid);
   const long long te = cta_begin(cta + 1, total, grid);
@@ -238,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
           const int y = lo + j * kTile, z = b * Hk + kvh;
           tma_load_3d(kst, &p.tmap_k, &full[s], 0, y * C::kHalves, z);
           tma_load_3d(kst + C::kTileBytes, &p.tmap_v, &full[s], 0, y * C::kHalves, z);
+          if (it == 0) DTRACE(5);
         }
         g += n;
       }
@@ -279,19 +298,51 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     const IO* row = qkv + static_cast<size_t>(b) * row_stride;
 
     // ---- segment setup: QK-norm + RoPE of the group's queries (and the new K/V)
-    for (int i = tid; i < G * D; i += 128) qf[i] = to_f32(row[kvh * G * D + i]);
-    if (has_new)
-      for (int i = tid; i < D; i += 128) {
-        kvf[i] = to_f32(row[(Hq + kvh) * D + i]);
-        kvf[D + i] = to_f32(row[(Hq + Hk + kvh) * D + i]);
+    // All global loads of the set-up go out together (read-only path) before
+    // any shared-memory store, so the set-up costs one memory round trip
+    // instead of one per loop trip.
+    {
+      constexpr int kQPer = 16 * D / 128;  // elements per thread for up to 16 query rows
+      float qv[kQPer];
+#pragma unroll
+      for (int u = 0; u < kQPer; ++u) {
+        const int i = tid + 128 * u;
+        qv[u] = i < G * D ? to_f32(__ldg(row + kvh * G * D + i)) : 0.f;
       }
-    for (int j = tid; j < half; j += 128) {
-      float c = 1.f, s = 0.f;
-      if (j < a.pair_count) rope_cos_sin(pos, a.inv_freq[j], &c, &s);
-      cs[j] = c;
-      cs[D / 2 + j] = s;
+      float kv0 = 0.f, kv1 = 0.f, kv2 = 0.f, kv3 = 0.f;  // the new K/V: D <= 256 values each
+      if (has_new) {
+        kv0 = to_f32(__ldg(row + (Hq + kvh) * D + tid));
+        kv1 = to_f32(__ldg(row + (Hq + Hk + kvh) * D + tid));
+        if (D > 128) {
+          kv2 = to_f32(__ldg(row + (Hq + kvh) * D + 128 + tid));
+          kv3 = to_f32(__ldg(row + (Hq + Hk + kvh) * D + 128 + tid));
+        }
+      }
+      const float f = (tid < half && tid < a.pair_count) ? __ldg(a.inv_freq + tid) : 0.f;
+#pragma unroll
+      for (int u = 0; u < kQPer; ++u) {
+        const int i = tid + 128 * u;
+        if (i < G * D) qf[i] = qv[u];
+      }
+      if (has_new) {
+        if (tid < D) {
+          kvf[tid] = kv0;
+          kvf[D + tid] = kv1;
+        }
+        if (D > 128) {
+          kvf[128 + tid] = kv2;
+          kvf[D + 128 + tid] = kv3;
+        }
+      }
+      if (tid < half) {  // half <= D / 2 <= 128
+        float c = 1.f, sn = 0.f;
+        if (tid < a.pair_count) rope_cos_sin(pos, f, &c, &sn);
+        cs[tid] = c;
+        cs[D / 2 + tid] = sn;
+      }
     }
     named_barrier_sync(1, 128);
+    if (tid == 0 && it == 0) DTRACE(7);
     for (int h = warp; h < G + 2; h += kConsumerWarps) {  // per-head RMS norms, math.ts:154-167
       const float* w;
       float* v;
@@ -319,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       }
     }
     named_barrier_sync(1, 128);
+    if (tid == 0 && it == 0) DTRACE(8);
     auto rope = [&](const float* v, int d) -> float {
       float val = v[d];
       if (d < a.rotary) {
@@ -358,6 +410,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    if (tid == 0 && it == 0) DTRACE(6);
 
     // ---- stream the segment's tiles
     for (int j = lt; j < lt + n; ++j, ++it) {
@@ -365,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       const uint32_t ph = (it / C::kStages) & 1u;
       if (!flags[0] && !mbar_wait(&full[s], ph, a.error)) flags[0] = 1;
       __syncwarp();
+      if (tid == 0 && it == 0) DTRACE(2);
       uint8_t* kst = stages + s * C::kStageBytes;
       uint8_t* vst = kst + C::kTileBytes;
       const int y0 = lo + j * kTile;
@@ -461,6 +515,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       if (lane == 0) mbar_arrive(&empty[s]);
     }
 
+    if (tid == 0) DTRACE(3);
     // ---- merge the 4 warps' (m, l, O)
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -637,6 +692,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     named_barrier_sync(1, 128);  // red / q_s / flags reuse by the next segment
     g += n;
   }
+  if (tid == 0) DTRACE(4);
 }
 
 // Deferred merge for pairs split across many CTAs (few, long sequences): one
@@ -1202,3 +1258,9 @@ extern "C" int tla_decode_noalloc(const tla_attn_config* cfg, void* key_cache, v
       launch_decode_fast(&L, qkv, positions, gate, out, nullptr, batch, 0, cfg->max_tokens, 1, st);
   return e == cudaSuccess ? TLA_OK : TLA_ERR_CUDA;
 }
+
+#ifdef TLA_DECODE_TRACE
+extern "C" int tla_debug_decode_trace(unsigned long long* host, int count) {
+  return cudaMemcpyFromSymbol(host, tla::g_decode_trace, sizeof(unsigned long long) * count) == cudaSuccess ? 0 : -1;
+}
+#endif
