@@ -696,10 +696,12 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
 }
 
 // Deferred merge for pairs split across many CTAs (few, long sequences): one
-// block of NT / 32 warps per (pair, query row); 16 warps when a pair spans 64
-// or more CTAs (one long sequence per kv head: up to the whole grid). The segment table (scratch slot and
+// block of 4 warps per (pair, query row); when a pair spans 64 or more CTAs
+// (one long sequence per kv head: up to the whole grid), one block of 16 warps
+// per (pair, query row, 32-column slice), so D / 32 times more SMs read the
+// segments. The segment table (scratch slot and
 // weight of every contributing CTA) is built once in shared memory; then warp
-// w sums segments w, w + NT / 32, ... with each lane holding D / 32 output columns,
+// w sums segments w, w + NT / 32, ... with each lane holding its output columns,
 // eight segments' loads in flight at a time, and the warps' partial rows are
 // added through shared memory. Pairs covered by a single CTA were written by
 // the decode kernel and are skipped.
@@ -710,16 +712,22 @@ template <int D, typename IO, int NT>
 __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant__ DecodeParams p,
                                                                      int grid) {
   constexpr int kWarps = NT / 32;
-  constexpr int kPer = D / 32;  // output columns per lane (float2 loads)
+  // 16-warp blocks take one 32-column slice of the row each (D / 32 blocks per
+  // row), so a pair split over the whole grid is read by D / 32 times more SMs
+  constexpr bool kSliced = NT >= 512;
+  constexpr int kSlices = kSliced ? D / 32 : 1;
+  constexpr int kCols = D / kSlices;  // output columns of this block
+  constexpr int kPer = kCols / 32;    // output columns per lane (float2 loads when 2)
   __shared__ long long prefix[kMaxBatch + 1];
   __shared__ int seg_slot[kMaxGrid];   // scratch slot of segment k, -1 if none
   __shared__ float seg_w[kMaxGrid];    // segment max, then its weight 2^(m - M)
   __shared__ float seg_l[kMaxGrid];    // segment sum
   __shared__ float red[2][kWarps];
-  __shared__ float rows_s[kWarps][D];
+  __shared__ float rows_s[kWarps][kCols];
   const LayerArgs& a = p.a;
   const int G = a.G, Hk = a.Hk;
-  const int pair = blockIdx.x / G, r = blockIdx.x - pair * G;
+  const int slice = static_cast<int>(blockIdx.x) % kSlices, row_id = static_cast<int>(blockIdx.x) / kSlices;
+  const int pair = row_id / G, r = row_id - pair * G;
   const int b = pair / Hk, kvh = pair - b * Hk;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // the decode kernel's partition, recomputed: tile counts in parallel, then a serial scan
@@ -784,54 +792,64 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
   float L = 0.f;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) L += red[1][w];
-  // rows are (D + 2) floats: 8-byte aligned, so float2 loads
-  const float2* col = reinterpret_cast<const float2*>(p.scratch + static_cast<size_t>(r) * (D + 2) + 2) + lane;
-  const size_t slot_stride2 = static_cast<size_t>(G) * (D + 2) / 2;
-  float2 acc[kPer / 2];
+  float acc0 = 0.f;
+  if constexpr (kPer >= 2) {
+    // rows are (D + 2) floats: 8-byte aligned, so float2 loads
+    const float2* col = reinterpret_cast<const float2*>(p.scratch + static_cast<size_t>(r) * (D + 2) + 2) + lane;
+    const size_t slot_stride2 = static_cast<size_t>(G) * (D + 2) / 2;
+    float2 acc[kPer / 2];
 #pragma unroll
-  for (int j = 0; j < kPer / 2; ++j) acc[j] = make_float2(0.f, 0.f);
-  int k = warp;
-  for (; k + 7 * kWarps < S; k += 8 * kWarps) {  // eight segments' loads in flight
-    float2 v[8][kPer / 2];
+    for (int j = 0; j < kPer / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+    for (int k = warp; k < S; k += 8 * kWarps) {  // eight segments' loads in flight (the last batch predicated)
+      float2 v[8][kPer / 2];
+      float wu[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int sl = seg_slot[k + u * kWarps];
+      for (int u = 0; u < 8; ++u) {
+        const int ku = k + u * kWarps;
+        const int sl = ku < S ? seg_slot[ku] : -1;
+        wu[u] = sl >= 0 ? seg_w[ku] : 0.f;
 #pragma unroll
-      for (int j = 0; j < kPer / 2; ++j)
-        v[u][j] = sl >= 0 ? __ldcg(col + static_cast<size_t>(sl) * slot_stride2 + j * 32) : make_float2(0.f, 0.f);
-    }
+        for (int j = 0; j < kPer / 2; ++j)
+          v[u][j] = sl >= 0 ? __ldcg(col + static_cast<size_t>(sl) * slot_stride2 + j * 32) : make_float2(0.f, 0.f);
+      }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const float w = seg_w[k + u * kWarps];
+      for (int u = 0; u < 8; ++u) {
 #pragma unroll
-      for (int j = 0; j < kPer / 2; ++j) {
-        acc[j].x += v[u][j].x * w;
-        acc[j].y += v[u][j].y * w;
+        for (int j = 0; j < kPer / 2; ++j) {
+          acc[j].x += v[u][j].x * wu[u];
+          acc[j].y += v[u][j].y * wu[u];
+        }
       }
     }
-  }
-  for (; k < S; k += kWarps) {
-    const int sl = seg_slot[k];
-    if (sl < 0) continue;
-    const float w = seg_w[k];
 #pragma unroll
     for (int j = 0; j < kPer / 2; ++j) {
-      const float2 v = __ldcg(col + static_cast<size_t>(sl) * slot_stride2 + j * 32);
-      acc[j].x += v.x * w;
-      acc[j].y += v.y * w;
+      rows_s[warp][2 * (lane + 32 * j)] = acc[j].x;
+      rows_s[warp][2 * (lane + 32 * j) + 1] = acc[j].y;
     }
-  }
+  } else {
+    const float* col = p.scratch + static_cast<size_t>(r) * (D + 2) + 2 + slice * kCols + lane;
+    const size_t slot_stride = static_cast<size_t>(G) * (D + 2);
+    for (int k = warp; k < S; k += 8 * kWarps) {
+      float v[8], wu[8];
 #pragma unroll
-  for (int j = 0; j < kPer / 2; ++j) {
-    rows_s[warp][2 * (lane + 32 * j)] = acc[j].x;
-    rows_s[warp][2 * (lane + 32 * j) + 1] = acc[j].y;
+      for (int u = 0; u < 8; ++u) {
+        const int ku = k + u * kWarps;
+        const int sl = ku < S ? seg_slot[ku] : -1;
+        wu[u] = sl >= 0 ? seg_w[ku] : 0.f;
+        v[u] = sl >= 0 ? __ldcg(col + static_cast<size_t>(sl) * slot_stride) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc0 += v[u] * wu[u];
+    }
+    rows_s[warp][lane] = acc0;
   }
   __syncthreads();
   const size_t hrow = static_cast<size_t>(b) * a.Hq + kvh * G + r;
-  for (int d = tid; d < D; d += NT) {
+  for (int c = tid; c < kCols; c += NT) {
     float o = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) o += rows_s[w][d];
+    for (int w = 0; w < kWarps; ++w) o += rows_s[w][c];
+    const int d = slice * kCols + c;
     if (p.partial_out) {
       p.partial_out[hrow * (D + 2) + 2 + d] = o;
       if (d == 0) {
@@ -1013,8 +1031,8 @@ cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, const ExchangeDe
   }
   if (!p.defer_merge) return e;
   const int pairs = p.batch * L->Hk;
-  if (L->decode_grid >= 64 * pairs)
-    decode_merge_kernel<D, IO, 512><<<pairs * L->G, 512, 0, stream>>>(p, L->decode_grid);
+  if (L->decode_grid >= 64 * pairs)  // 16 warps per block, one 32-column slice per block
+    decode_merge_kernel<D, IO, 512><<<pairs * L->G * (D / 32), 512, 0, stream>>>(p, L->decode_grid);
   else
     decode_merge_kernel<D, IO, kMergeThreads><<<pairs * L->G, kMergeThreads, 0, stream>>>(p, L->decode_grid);
   return cudaGetLastError();
