@@ -164,6 +164,10 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int grid = gridDim.x, cta = blockIdx.x;
   if (tid == 0) DTRACE(0);
+  // inputs (positions, qkv, the cache, the scratch) may come from the previous
+  // kernel; once they are visible, the next kernel may start its prologue
+  griddep_wait();
+  griddep_launch_dependents();
 
   // ---- partition: tiles per sequence, prefix over (sequence, kv head) pairs
   for (int b = tid; b < p.batch; b += kThreads) {
@@ -757,11 +761,25 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
   const int c0 = cta_of(pb, total, grid), c1 = cta_of(pb + tiles - 1, total, grid);
   if (c0 == c1) return;  // one CTA held the whole pair
   const int S = c1 - c0 + 1;
+  int slots[kMaxGrid / NT];  // this thread's segments: computed before the decode kernel has finished
+#pragma unroll
+  for (int u = 0; u < kMaxGrid / NT; ++u) {
+    const int k = tid + u * NT;
+    slots[u] = -1;
+    if (k < S) {
+      const int c = c0 + k;
+      const long long cb = cta_begin(c, total, grid);
+      slots[u] = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
+    }
+  }
+  griddep_wait();  // the decode kernel's segments are complete and visible
+  griddep_launch_dependents();
   float m = -INFINITY;
-  for (int k = tid; k < S; k += NT) {
-    const int c = c0 + k;
-    const long long cb = cta_begin(c, total, grid);
-    const int sl = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
+#pragma unroll
+  for (int u = 0; u < kMaxGrid / NT; ++u) {
+    const int k = tid + u * NT;
+    if (k >= S) break;
+    const int sl = slots[u];
     seg_slot[k] = sl;
     float mk = -INFINITY, lk = 0.f;
     if (sl >= 0) {
@@ -908,6 +926,8 @@ __global__ void __launch_bounds__(kMergeThreads) decode_exchange_kernel(const __
       prefix[bb] = acc;
     }
   }
+  griddep_wait();  // the decode kernel's segments are complete and visible
+  griddep_launch_dependents();
   const unsigned epoch = xch_epoch(x, &epoch_s);  // syncs the block
   const long long total = prefix[p.batch];
   const int rows = p.batch * Hq;
@@ -1017,25 +1037,41 @@ __global__ void __launch_bounds__(kMergeThreads) decode_exchange_kernel(const __
   xch_finish(x, epoch);
 }
 
+// Launch with programmatic dependent launch allowed: the kernel may start
+// while the previous kernel in the stream finishes; it waits (griddep_wait)
+// before touching anything that kernel produces.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <int D, typename IO, bool TWO>
 cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, const ExchangeDev* x, cudaStream_t stream) {
   const SmemLayout s = smem_layout<D>(L->G, p.batch);
-  decode_fast_kernel<D, IO, TWO><<<L->decode_grid, kThreads, s.total, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(decode_fast_kernel<D, IO, TWO>, L->decode_grid, kThreads, s.total, stream, p);
   if (e != cudaSuccess) return e;
   if (x != nullptr) {
     const int rows = p.batch * L->Hq;
     const int grid = rows < L->ctx->sm_count ? rows : L->ctx->sm_count;
-    decode_exchange_kernel<D, IO><<<grid, kMergeThreads, 0, stream>>>(p, L->decode_grid, *x);
-    return cudaGetLastError();
+    return launch_pdl(decode_exchange_kernel<D, IO>, grid, kMergeThreads, 0, stream, p, L->decode_grid, *x);
   }
   if (!p.defer_merge) return e;
   const int pairs = p.batch * L->Hk;
   if (L->decode_grid >= 64 * pairs)  // 16 warps per block, one 32-column slice per block
-    decode_merge_kernel<D, IO, 512><<<pairs * L->G * (D / 32), 512, 0, stream>>>(p, L->decode_grid);
-  else
-    decode_merge_kernel<D, IO, kMergeThreads><<<pairs * L->G, kMergeThreads, 0, stream>>>(p, L->decode_grid);
-  return cudaGetLastError();
+    return launch_pdl(decode_merge_kernel<D, IO, 512>, pairs * L->G * (D / 32), 512, 0, stream, p, L->decode_grid);
+  return launch_pdl(decode_merge_kernel<D, IO, kMergeThreads>, pairs * L->G, kMergeThreads, 0, stream, p,
+                    L->decode_grid);
 }
 
 template <int D, typename IO, bool TWO>

@@ -113,6 +113,14 @@ __device__ __forceinline__ bool mbar_nap(uint64_t* bar, uint32_t parity, int* er
   }
 }
 
+// Programmatic dependent launch: wait for the preceding kernel in the stream
+// (complete, memory visible); let the following kernel start its prologue.
+// Both are no-ops for a kernel not launched with the PDL attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
