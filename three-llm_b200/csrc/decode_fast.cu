@@ -1037,25 +1037,6 @@ __global__ void __launch_bounds__(kMergeThreads) decode_exchange_kernel(const __
   xch_finish(x, epoch);
 }
 
-// Launch with programmatic dependent launch allowed: the kernel may start
-// while the previous kernel in the stream finishes; it waits (griddep_wait)
-// before touching anything that kernel produces.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
-                       Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(block);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, args...);
-}
-
 template <int D, typename IO, bool TWO>
 cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, const ExchangeDev* x, cudaStream_t stream) {
   const SmemLayout s = smem_layout<D>(L->G, p.batch);

@@ -378,6 +378,7 @@ __global__ void __launch_bounds__(128) rope_rows_kernel(LayerArgs a, const __hal
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int ti = blockIdx.x * 4 + (threadIdx.x >> 5);
+  griddep_wait();  // qkv, start and the cache may come from the previous kernel
   if (ti >= tokens) return;
   const int b = ti / seq_len, t = ti - b * seq_len;
   const int Hq = a.Hq, Hk = a.Hk, heads = Hq + 2 * Hk;
@@ -471,15 +472,15 @@ __global__ void __launch_bounds__(128) rope_rows_kernel(LayerArgs a, const __hal
       *reinterpret_cast<uint4*>(dst) = outv;
     }
   }
+  griddep_launch_dependents();  // the attention kernel may start its prologue
 }
 
 template <int D>
 cudaError_t rope_rows_t(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
                         __half* qscr, cudaStream_t stream) {
   const int tokens = batch * seq_len;
-  rope_rows_kernel<D><<<(tokens + 3) / 4, 128, 0, stream>>>(layer_args(L), static_cast<const __half*>(qkv), start,
-                                                            seq_len, tokens, qscr);
-  return cudaGetLastError();
+  return launch_pdl(rope_rows_kernel<D>, (tokens + 3) / 4, 128, 0, stream, layer_args(L),
+                    static_cast<const __half*>(qkv), start, seq_len, tokens, qscr);
 }
 
 template <typename IO, int D>

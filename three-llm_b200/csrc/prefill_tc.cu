@@ -298,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // the RoPE/append kernel's queries and cache rows are complete
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     if (*abort_flag) return;
     if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
@@ -619,14 +620,14 @@ cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32
   const dim3 grid(static_cast<unsigned>(items < L->ctx->sm_count ? items : L->ctx->sm_count));
   if (L->D == 64) {
     if (L->io_fp32)
-      prefill_tc_kernel<64, float><<<grid, kThreads, PCfg<64>::kSmem, stream>>>(p);
+      return launch_pdl(prefill_tc_kernel<64, float>, grid.x, kThreads, PCfg<64>::kSmem, stream, p);
     else
-      prefill_tc_kernel<64, __half><<<grid, kThreads, PCfg<64>::kSmem, stream>>>(p);
+      return launch_pdl(prefill_tc_kernel<64, __half>, grid.x, kThreads, PCfg<64>::kSmem, stream, p);
   } else {
     if (L->io_fp32)
-      prefill_tc_kernel<128, float><<<grid, kThreads, PCfg<128>::kSmem, stream>>>(p);
+      return launch_pdl(prefill_tc_kernel<128, float>, grid.x, kThreads, PCfg<128>::kSmem, stream, p);
     else
-      prefill_tc_kernel<128, __half><<<grid, kThreads, PCfg<128>::kSmem, stream>>>(p);
+      return launch_pdl(prefill_tc_kernel<128, __half>, grid.x, kThreads, PCfg<128>::kSmem, stream, p);
   }
   return cudaGetLastError();
 }

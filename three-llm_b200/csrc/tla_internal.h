@@ -53,6 +53,26 @@ struct tla_layer {
 
 namespace tla {
 
+// Launch with programmatic dependent launch allowed: the kernel may start
+// while the previous kernel in the stream finishes; it waits (griddep_wait)
+// before touching anything that kernel produces.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+
 // Parameters shared by all decode / prefill kernels of one layer.
 struct LayerArgs {
   void* k_cache;
