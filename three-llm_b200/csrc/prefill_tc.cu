@@ -431,6 +431,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const float sl2 = p.scale_log2;
     int g = 0;
+    // The completion wait of a step's P stores and its p_full arrival are
+    // deferred until the next step's S is loaded, so the TMEM store and load
+    // latencies overlap (different S buffers; the MMA issuer only needs P(g)
+    // before P V(g)).
+    int pend_j = -1;
+    auto release_p = [&]() {
+      if (pend_j >= 0) {
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[pend_j]);
+        pend_j = -1;
+      }
+    };
     for (int k = 0;; ++k) {
       const int it = prefill_item_of(k, num_items);
       if (it < 0) break;
@@ -449,6 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         uint32_t sv[128];
         tmem_ld64x(buf, *reinterpret_cast<uint32_t(*)[64]>(&sv[0]));
         tmem_ld64x(buf + 64, *reinterpret_cast<uint32_t(*)[64]>(&sv[64]));
+        release_p();  // the previous step's P (its P V may now be issued)
         const int tok0 = (w.j0 + n) * kT;
         const bool masked = tok0 + kT - 1 > pr || tok0 < first_r;
         const int lo = first_r - tok0, hi = pr - tok0;  // valid columns [lo, hi]
@@ -506,11 +520,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           }
           tmem_st32(buf + 32 * c, pk);
         }
-        tmem_wait_st();
         l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
-        tc_fence_before();
-        mbar_arrive(&p_full[j]);
+        pend_j = j;
       }
+      release_p();
       // ---- item epilogue: normalise and store this row's outputs, then free O
       // the last step waited for P V(g-3); now P V(g-2) and P V(g-1)
       if (g >= 2) wait(&o_done[g & 1], ((g - 2) >> 1) & 1);
