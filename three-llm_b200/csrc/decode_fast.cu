@@ -53,14 +53,29 @@ constexpr int kMaxBatch = 1024;      // prefix table in shared memory
 // Optional per-CTA timeline (builds with -DTLA_DECODE_TRACE only): globaltimer
 // at [cta][0] entry, [1] partition done, [2] first tile landed (consumer warp
 // 0), [3] last tile consumed, [4] exit, [5] first TMA issued, [6] first
-// segment's query set-up done; read with tla_debug_decode_trace.
-__device__ unsigned long long g_decode_trace[2048][10];
+// segment's query set-up done, [7] set-up loads stored, [8] norms done,
+// [10] query rows stored, [11] RoPE factors stored, [12] RoPE applied,
+// [13] producer has the first position, [14] partition re-checked after the
+// wait, [15] consumer has the first position; read with
+// tla_debug_decode_trace. The timer read is a compiler memory barrier, so an
+// event follows the memory operations before it in program order.
+__device__ unsigned long long g_decode_trace[2048][16];
 #define DTRACE(ev) \
   do { \
-    if (blockIdx.x < 2048) g_decode_trace[blockIdx.x][(ev)] = globaltimer(); \
+    unsigned long long t_; \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)::"memory"); \
+    if (blockIdx.x < 2048) g_decode_trace[blockIdx.x][(ev)] = t_; \
+  } while (0)
+#define DTRACE_AFTER(ev, v) \
+  do { \
+    asm volatile("" ::"r"(v)); \
+    DTRACE(ev); \
   } while (0)
 #else
 #define DTRACE(ev) \
+  do { \
+  } while (0)
+#define DTRACE_AFTER(ev, v) \
   do { \
   } while (0)
 #endif
@@ -94,7 +109,7 @@ struct DecodeParams {
 
 struct SmemLayout {
   // byte offsets from the 1024-aligned base
-  int stages, q, qf, kvf, cs, newkv, red, prefix, bars, flags, total;
+  int stages, q, qf, kvf, cs, newkv, red, prefix, spos, bars, flags, total;
 };
 
 template <int D>
@@ -118,6 +133,8 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int batch) {
   off += kConsumerWarps * G * (D + 2) * 4;
   s.prefix = off;
   off += (batch + 1) * 4;
+  s.spos = off;  // the positions, as read after the wait
+  off += batch * 4;
   off = (off + 7) & ~7;
   s.bars = off;
   off += 2 * C::kStages * 8;
@@ -148,6 +165,104 @@ __device__ __forceinline__ int cta_of(long long g, long long total, int grid) {
   return c;
 }
 
+// Tiles of a sequence at position pos in this launch (0 when the position is
+// invalid; *ok says whether it was valid). With append, the new token must be the last
+// local slot (always true for plain decode, where the local range is the whole
+// cache).
+__device__ __forceinline__ int pair_tiles(const DecodeParams& p, int pos, bool* ok_out) {
+  const LayerArgs& a = p.a;
+  int lo, hi;
+  seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
+  const bool ok = pos >= 0 && (p.partial_out != nullptr || pos < a.max_tokens) &&
+                  (!p.append || (pos - p.slot_offset >= 0 && pos - p.slot_offset < a.max_tokens &&
+                                 pos - p.slot_offset == hi));
+  if (ok_out) *ok_out = ok;
+  return ok && hi >= lo ? (hi - lo + kTile) / kTile : 0;
+}
+
+// Inclusive scan of prefix[1..batch] by warp 0 (prefix[0] = 0).
+__device__ __forceinline__ void scan_prefix(int* prefix, int batch, int warp, int lane) {
+  if (warp != 0) return;
+  int carry = 0;
+  for (int base = 1; base <= batch; base += 32) {
+    const int i = base + lane;
+    int v = i <= batch ? prefix[i] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
+    }
+    if (i <= batch) prefix[i] = v + carry;
+    carry += __shfl_sync(0xffffffffu, v, 31);
+  }
+}
+
+// L2 prefetch of the K and V boxes of this CTA's first kPrefetchTiles tiles
+// under the given partition (a hint only: the tensor maps bound every box).
+constexpr int kPrefetchTiles = 4;
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+template <int D>
+__device__ __forceinline__ void prefetch_first_tiles(const DecodeParams& p, const int* prefix, int cta, int grid) {
+  const long long total = prefix[p.batch];
+  if (total == 0) return;
+  const long long tb = cta_begin(cta, total, grid), te = cta_begin(cta + 1, total, grid);
+  const int Hk = p.a.Hk;
+  int b = 0, done = 0;
+  for (long long g = tb; g < te && done < kPrefetchTiles;) {
+    while (prefix[b + 1] <= g) ++b;
+    const int tiles = (prefix[b + 1] - prefix[b]) / Hk;
+    const int off = static_cast<int>(g - prefix[b]);
+    const int kvh = off / tiles, lt = off - kvh * tiles;
+    const int n = static_cast<int>(min(te - g, static_cast<long long>(tiles - lt)));
+    int lo, hi;
+    seq_range(p.a, p.positions[b], p.slot_offset, p.local_tokens, &lo, &hi);
+    for (int j = lt; j < lt + n && done < kPrefetchTiles; ++j, ++done) {
+      const int y = (lo + j * kTile) * Cfg<D>::kHalves, z = b * Hk + kvh;
+      tma_prefetch_l2_3d(&p.tmap_k, 0, y, z);
+      tma_prefetch_l2_3d(&p.tmap_v, 0, y, z);
+    }
+    g += n;
+  }
+}
+
+// L2 prefetch of the set-up inputs of this CTA's first segment (the group's
+// query rows, the new K/V rows, the RoPE frequencies) by the consumer
+// threads, from the speculative partition, before the wait. A hint only: L2
+// receives the previous kernel's writes, so no stale line survives there.
+// (An L1 prefetch after the wait was measured slower.)
+template <int D, typename IO>
+__device__ __forceinline__ void prefetch_first_rows(const DecodeParams& p, const int* prefix, int cta, int grid,
+                                                    int tid) {
+  const long long total = prefix[p.batch];
+  if (total == 0) return;
+  const long long tb = cta_begin(cta, total, grid), te = cta_begin(cta + 1, total, grid);
+  if (tb >= te) return;
+  const LayerArgs& a = p.a;
+  int b = 0;
+  while (prefix[b + 1] <= tb) ++b;
+  const int tiles = (prefix[b + 1] - prefix[b]) / a.Hk;
+  const int off = static_cast<int>(tb - prefix[b]);
+  const int kvh = off / tiles;
+  const char* row = static_cast<const char*>(p.qkv) + static_cast<size_t>(b) * (a.Hq + 2 * a.Hk) * D * sizeof(IO);
+  constexpr int kRowLines = D * sizeof(IO) / 128;  // 128-byte lines per head row (D * sizeof(IO) >= 128)
+  const int q_lines = a.G * kRowLines;
+  const char* addr = nullptr;
+  if (tid < q_lines) {
+    addr = row + (static_cast<size_t>(kvh) * a.G * D) * sizeof(IO) + tid * 128;
+  } else if (tid < q_lines + 2 * kRowLines) {
+    const int i = tid - q_lines, which = i / kRowLines;
+    addr = row + (static_cast<size_t>(a.Hq + which * a.Hk + kvh) * D) * sizeof(IO) + (i - which * kRowLines) * 128;
+  } else if (tid < q_lines + 2 * kRowLines + 2 && a.inv_freq != nullptr) {
+    addr = reinterpret_cast<const char*>(a.inv_freq) + (tid - q_lines - 2 * kRowLines) * 128;
+  }
+  if (addr) asm volatile("prefetch.global.L2 [%0];" ::"l"(addr));
+}
+
 template <int D, typename IO, bool TWO_ROWS>
 __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     decode_fast_kernel(const __grid_constant__ DecodeParams p) {
@@ -164,31 +279,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int grid = gridDim.x, cta = blockIdx.x;
   if (tid == 0) DTRACE(0);
-  // inputs (positions, qkv, the cache, the scratch) may come from the previous
-  // kernel; once they are visible, the next kernel may start its prologue
-  griddep_wait();
-  griddep_launch_dependents();
-
-  // ---- partition: tiles per sequence, prefix over (sequence, kv head) pairs
-  for (int b = tid; b < p.batch; b += kThreads) {
-    const int pos = p.positions[b];
-    int tiles = 0;
-    int lo, hi;
-    seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
-    // With append, the new token must be the last local slot (always true
-    // for plain decode, where the local range is the whole cache).
-    const bool ok = pos >= 0 && (p.partial_out != nullptr || pos < a.max_tokens) &&
-                    (!p.append || (pos - p.slot_offset >= 0 && pos - p.slot_offset < a.max_tokens &&
-                                   pos - p.slot_offset == hi));
-    if (ok) {
-      if (hi >= lo) tiles = (hi - lo + kTile) / kTile;
-    } else if (cta == 0) {
-      report_error(a.error, TLA_ERR_POSITION);
-    }
-    prefix[b + 1] = tiles * Hk;
-  }
   if (tid == 0) {
-    prefix[0] = 0;
     flags[0] = 0;
     flags[1] = 0;
     for (int s = 0; s < C::kStages; ++s) {
@@ -197,22 +288,49 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     }
     fence_mbar_init();
   }
+  // ---- partition: tiles per sequence, prefix over (sequence, kv head) pairs.
+  // It is first built from the positions as they read while the previous
+  // kernel may still be running, and only used to prefetch this CTA's first
+  // tiles into L2 (a prefetch cannot return stale data: L2 is where writes
+  // land); after the wait the positions are read again and the partition is
+  // rebuilt only if one of them changed.
+  for (int b = tid; b < p.batch; b += kThreads) prefix[b + 1] = pair_tiles(p, p.positions[b], nullptr) * Hk;
+  if (tid == 0) prefix[0] = 0;
   __syncthreads();
-  if (warp == 0) {  // inclusive scan of prefix[1..batch]
-    int carry = 0;
-    for (int base = 1; base <= p.batch; base += 32) {
-      const int i = base + lane;
-      int v = i <= p.batch ? prefix[i] : 0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += n;
-      }
-      if (i <= p.batch) prefix[i] = v + carry;
-      carry += __shfl_sync(0xffffffffu, v, 31);
+  scan_prefix(prefix, p.batch, warp, lane);
+  __syncthreads();
+  if (warp == kConsumerWarps) {
+    if (lane == 0) prefetch_first_tiles<D>(p, prefix, cta, grid);
+  } else {
+    prefetch_first_rows<D, IO>(p, prefix, cta, grid, tid);
+    // rows G..15 of the query tile stay zero (the m16 MMA's padding rows)
+    __half* q_pad = reinterpret_cast<__half*>(smem + L.q);
+    for (int i = tid; i < (16 - G) * D; i += kConsumerWarps * 32) {
+      const int r = G + i / D, d = i - (i / D) * D;
+      q_pad[r * (C::kQPitch / 2) + d] = __float2half_rn(0.f);
     }
   }
-  __syncthreads();
+  // inputs (positions, qkv, the cache, the scratch) may come from the previous
+  // kernel; once they are visible, the next kernel may start its prologue
+  griddep_wait();
+  griddep_launch_dependents();
+  int* spos = reinterpret_cast<int*>(smem + L.spos);
+  bool changed = false;
+  for (int b = tid; b < p.batch; b += kThreads) {
+    bool ok;
+    const int pos = p.positions[b];
+    spos[b] = pos;
+    const int tiles = pair_tiles(p, pos, &ok);
+    if (!ok && cta == 0) report_error(a.error, TLA_ERR_POSITION);
+    changed |= tiles * Hk != prefix[b + 1] - prefix[b];
+  }
+  if (__syncthreads_or(changed)) {
+    for (int b = tid; b < p.batch; b += kThreads) prefix[b + 1] = pair_tiles(p, spos[b], nullptr) * Hk;
+    __syncthreads();
+    scan_prefix(prefix, p.batch, warp, lane);
+    __syncthreads();
+  }
+  if (tid == 0) DTRACE(14);
   const long long total = prefix[p.batch];
 
   // Sequence-shard mode: pairs with no local tokens still emit an empty triple.
@@ -247,7 +365,8 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         const int kvh = off / tiles, lt = off - kvh * tiles;
         const int n = static_cast<int>(min(te - g, static_cast<long long>(tiles - lt)));
         int lo, hi;
-        seq_range(a, p.positions[b], p.slot_offset, p.local_tokens, &lo, &hi);
+        seq_range(a, spos[b], p.slot_offset, p.local_tokens, &lo, &hi);
+        if (it == 0) DTRACE(13);
         for (int j = lt; j < lt + n; ++j, ++it) {
           const int s = it % C::kStages;
           const uint32_t ph = (it / C::kStages) & 1u;
@@ -294,10 +413,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     const int off = static_cast<int>(g - prefix[b]);
     const int kvh = off / tiles, lt = off - kvh * tiles;
     const int n = static_cast<int>(min(te - g, static_cast<long long>(tiles - lt)));
-    const int pos = p.positions[b];
+    const int pos = spos[b];
     int lo, hi;
     seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
     const int slot_new = pos - p.slot_offset;
+    if (tid == 0 && it == 0) DTRACE_AFTER(15, pos);
     const bool has_new = p.append && (lt + n == tiles);
     const IO* row = qkv + static_cast<size_t>(b) * row_stride;
 
@@ -328,6 +448,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         const int i = tid + 128 * u;
         if (i < G * D) qf[i] = qv[u];
       }
+      if (tid == 0 && it == 0) DTRACE(10);
       if (has_new) {
         if (tid < D) {
           kvf[tid] = kv0;
@@ -344,6 +465,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         cs[tid] = c;
         cs[D / 2 + tid] = sn;
       }
+      if (tid == 0 && it == 0) DTRACE(11);
     }
     named_barrier_sync(1, 128);
     if (tid == 0 && it == 0) DTRACE(7);
@@ -386,9 +508,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       }
       return val;
     };
-    for (int i = tid; i < 16 * D; i += 128) {
+    for (int i = tid; i < G * D; i += 128) {  // rows G..15 were zeroed at the start
       const int r = i / D, d = i - r * D;
-      q_s[r * (C::kQPitch / 2) + d] = __float2half_rn(r < G ? rope(qf + r * D, d) : 0.f);
+      q_s[r * (C::kQPitch / 2) + d] = __float2half_rn(rope(qf + r * D, d));
     }
     if (has_new)
       for (int d = tid; d < D; d += 128) {
@@ -402,6 +524,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       reinterpret_cast<uint4*>(static_cast<__half*>(a.v_cache) + base)[0] =
           reinterpret_cast<const uint4*>(newkv + D)[tid];
     }
+    if (tid == 0 && it == 0) DTRACE(12);
     uint32_t qa[D / 16][4];
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
@@ -703,12 +826,13 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
 // block of 4 warps per (pair, query row); when a pair spans 64 or more CTAs
 // (one long sequence per kv head: up to the whole grid), one block of 16 warps
 // per (pair, query row, 32-column slice), so D / 32 times more SMs read the
-// segments. The segment table (scratch slot and
-// weight of every contributing CTA) is built once in shared memory; then warp
-// w sums segments w, w + NT / 32, ... with each lane holding its output columns,
-// eight segments' loads in flight at a time, and the warps' partial rows are
-// added through shared memory. Pairs covered by a single CTA were written by
-// the decode kernel and are skipped.
+// segments. The segment table (the scratch slot of every contributing CTA)
+// is built in shared memory before the decode kernel has finished; then, in
+// one pass, warp w folds segments w, w + NT / 32, ... into a running triple
+// (maximum, sum, this lane's output columns) with 8 or 12 segments' loads in
+// flight at a time, and the warps' triples are combined through shared memory.
+// Pairs covered by a single CTA were written by the decode kernel and are
+// skipped.
 constexpr int kMaxGrid = 16 * 128;  // the host keeps decode_grid <= 16 * D
 constexpr int kMergeThreads = 128;
 
@@ -724,8 +848,6 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
   constexpr int kPer = kCols / 32;    // output columns per lane (float2 loads when 2)
   __shared__ long long prefix[kMaxBatch + 1];
   __shared__ int seg_slot[kMaxGrid];   // scratch slot of segment k, -1 if none
-  __shared__ float seg_w[kMaxGrid];    // segment max, then its weight 2^(m - M)
-  __shared__ float seg_l[kMaxGrid];    // segment sum
   __shared__ float red[2][kWarps];
   __shared__ float rows_s[kWarps][kCols];
   const LayerArgs& a = p.a;
@@ -761,112 +883,97 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
   const int c0 = cta_of(pb, total, grid), c1 = cta_of(pb + tiles - 1, total, grid);
   if (c0 == c1) return;  // one CTA held the whole pair
   const int S = c1 - c0 + 1;
-  int slots[kMaxGrid / NT];  // this thread's segments: computed before the decode kernel has finished
-#pragma unroll
-  for (int u = 0; u < kMaxGrid / NT; ++u) {
-    const int k = tid + u * NT;
-    slots[u] = -1;
-    if (k < S) {
-      const int c = c0 + k;
-      const long long cb = cta_begin(c, total, grid);
-      slots[u] = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
-    }
+  // the segment table (computed before the decode kernel has finished)
+  for (int k = tid; k < S; k += NT) {
+    const int c = c0 + k;
+    const long long cb = cta_begin(c, total, grid);
+    seg_slot[k] = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
   }
+  __syncthreads();
   griddep_wait();  // the decode kernel's segments are complete and visible
   griddep_launch_dependents();
-  float m = -INFINITY;
+  // One pass: warp w folds segments w, w + NT / 32, ... with a running
+  // maximum (the online softmax across segments), loading the triples of kB
+  // segments at once; then the warps' partial triples are combined.
+  constexpr int kB = kSliced ? 12 : 8;
+  const float* rowp = p.scratch + static_cast<size_t>(r) * (D + 2);
+  const size_t slot_stride = static_cast<size_t>(G) * (D + 2);
+  float mw = -INFINITY, lw = 0.f;
+  float acc[kPer];
 #pragma unroll
-  for (int u = 0; u < kMaxGrid / NT; ++u) {
-    const int k = tid + u * NT;
-    if (k >= S) break;
-    const int sl = slots[u];
-    seg_slot[k] = sl;
-    float mk = -INFINITY, lk = 0.f;
-    if (sl >= 0) {
-      const float* sp = p.scratch + (static_cast<size_t>(sl) * G + r) * (D + 2);
-      mk = __ldcg(sp);
-      lk = __ldcg(sp + 1);
+  for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+  for (int k = warp; k < S; k += kB * kWarps) {
+    float mk[kB], lk[kB], v[kB][kPer];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int ku = k + u * kWarps;
+      const int sl = ku < S ? seg_slot[ku] : -1;
+      mk[u] = -INFINITY;
+      lk[u] = 0.f;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) v[u][j] = 0.f;
+      if (sl >= 0) {
+        const float* sp = rowp + static_cast<size_t>(sl) * slot_stride;
+        mk[u] = __ldcg(sp);
+        lk[u] = __ldcg(sp + 1);
+        if constexpr (kPer >= 2) {
+#pragma unroll
+          for (int j = 0; j < kPer / 2; ++j) {
+            const float2 t = __ldcg(reinterpret_cast<const float2*>(sp + 2) + lane + 32 * j);
+            v[u][2 * j] = t.x;
+            v[u][2 * j + 1] = t.y;
+          }
+        } else {
+          v[u][0] = __ldcg(sp + 2 + slice * kCols + lane);
+        }
+      }
     }
-    seg_w[k] = mk;
-    seg_l[k] = lk;
-    m = fmaxf(m, mk);
-  }
+    float mb = mw;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) red[0][warp] = m;
+    for (int u = 0; u < kB; ++u) mb = fmaxf(mb, mk[u]);
+    if (mb == -INFINITY) continue;
+    const float sc = mw == -INFINITY ? 0.f : ex2(mw - mb);
+    lw *= sc;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) acc[j] *= sc;
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const float w = mk[u] == -INFINITY ? 0.f : ex2(mk[u] - mb);
+      lw += lk[u] * w;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) acc[j] += v[u][j] * w;
+    }
+    mw = mb;
+  }
+  if (lane == 0) {
+    red[0][warp] = mw;
+    red[1][warp] = lw;
+  }
+  if constexpr (kPer >= 2) {
+#pragma unroll
+    for (int j = 0; j < kPer / 2; ++j) {
+      rows_s[warp][2 * (lane + 32 * j)] = acc[2 * j];
+      rows_s[warp][2 * (lane + 32 * j) + 1] = acc[2 * j + 1];
+    }
+  } else {
+    rows_s[warp][lane] = acc[0];
+  }
   __syncthreads();
   float M = red[0][0];
 #pragma unroll
   for (int w = 1; w < kWarps; ++w) M = fmaxf(M, red[0][w]);
-  float l = 0.f;
-  for (int k = tid; k < S; k += NT) {
-    const float w = (seg_slot[k] < 0 || M == -INFINITY) ? 0.f : ex2(seg_w[k] - M);
-    seg_w[k] = w;
-    l += seg_l[k] * w;
-  }
-  l = warp_sum(l);
-  if (lane == 0) red[1][warp] = l;
-  __syncthreads();
+  float wt[kWarps];
   float L = 0.f;
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) L += red[1][w];
-  float acc0 = 0.f;
-  if constexpr (kPer >= 2) {
-    // rows are (D + 2) floats: 8-byte aligned, so float2 loads
-    const float2* col = reinterpret_cast<const float2*>(p.scratch + static_cast<size_t>(r) * (D + 2) + 2) + lane;
-    const size_t slot_stride2 = static_cast<size_t>(G) * (D + 2) / 2;
-    float2 acc[kPer / 2];
-#pragma unroll
-    for (int j = 0; j < kPer / 2; ++j) acc[j] = make_float2(0.f, 0.f);
-    for (int k = warp; k < S; k += 8 * kWarps) {  // eight segments' loads in flight (the last batch predicated)
-      float2 v[8][kPer / 2];
-      float wu[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int ku = k + u * kWarps;
-        const int sl = ku < S ? seg_slot[ku] : -1;
-        wu[u] = sl >= 0 ? seg_w[ku] : 0.f;
-#pragma unroll
-        for (int j = 0; j < kPer / 2; ++j)
-          v[u][j] = sl >= 0 ? __ldcg(col + static_cast<size_t>(sl) * slot_stride2 + j * 32) : make_float2(0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-#pragma unroll
-        for (int j = 0; j < kPer / 2; ++j) {
-          acc[j].x += v[u][j].x * wu[u];
-          acc[j].y += v[u][j].y * wu[u];
-        }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kPer / 2; ++j) {
-      rows_s[warp][2 * (lane + 32 * j)] = acc[j].x;
-      rows_s[warp][2 * (lane + 32 * j) + 1] = acc[j].y;
-    }
-  } else {
-    const float* col = p.scratch + static_cast<size_t>(r) * (D + 2) + 2 + slice * kCols + lane;
-    const size_t slot_stride = static_cast<size_t>(G) * (D + 2);
-    for (int k = warp; k < S; k += 8 * kWarps) {
-      float v[8], wu[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int ku = k + u * kWarps;
-        const int sl = ku < S ? seg_slot[ku] : -1;
-        wu[u] = sl >= 0 ? seg_w[ku] : 0.f;
-        v[u] = sl >= 0 ? __ldcg(col + static_cast<size_t>(sl) * slot_stride) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) acc0 += v[u] * wu[u];
-    }
-    rows_s[warp][lane] = acc0;
+  for (int w = 0; w < kWarps; ++w) {
+    wt[w] = red[0][w] == -INFINITY ? 0.f : ex2(red[0][w] - M);
+    L += red[1][w] * wt[w];
   }
-  __syncthreads();
   const size_t hrow = static_cast<size_t>(b) * a.Hq + kvh * G + r;
   for (int c = tid; c < kCols; c += NT) {
     float o = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) o += rows_s[w][c];
+    for (int w = 0; w < kWarps; ++w) o += rows_s[w][c] * wt[w];
     const int d = slice * kCols + c;
     if (p.partial_out) {
       p.partial_out[hrow * (D + 2) + 2 + d] = o;
