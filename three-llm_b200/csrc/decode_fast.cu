@@ -165,6 +165,38 @@ __device__ __forceinline__ int cta_of(long long g, long long total, int grid) {
   return c;
 }
 
+// The stream-K split is over partition units: every (sequence, kv head) pair
+// with tiles takes kSetupUnits units before its tiles, so a CTA that starts
+// several pairs (each with a query set-up and an epilogue, measured at about
+// two 64-token tiles of streaming at head_dim 128) gets fewer tiles.
+template <int D>
+struct Units {
+  static constexpr int kSetup = D == 64 ? 4 : 2;
+};
+
+// The pair holding unit g of sequence b (prefix[b] <= g < prefix[b + 1]) and
+// this CTA's share of it, for a CTA whose range ends at te.
+struct Seg {
+  int kvh, tiles, lt, n;  // n: this CTA's tiles of the pair, from tile lt (may be 0)
+  long long start;        // the pair's first unit (its set-up units included)
+  long long first_tile;   // the unit of its tile 0
+  long long next;         // where this CTA's next pair starts
+};
+template <typename PT>
+__device__ __forceinline__ Seg seg_at(const PT* prefix, int b, int Hk, int setup, long long g, long long te) {
+  Seg sg;
+  const int per = static_cast<int>((prefix[b + 1] - prefix[b]) / Hk);  // units per pair: tiles + setup
+  sg.tiles = per - setup;
+  sg.kvh = static_cast<int>((g - prefix[b]) / per);
+  sg.start = prefix[b] + static_cast<long long>(sg.kvh) * per;
+  sg.first_tile = sg.start + setup;
+  const long long end = min(te, sg.first_tile + sg.tiles);
+  sg.lt = static_cast<int>(max(0LL, g - sg.first_tile));
+  sg.n = static_cast<int>(max(0LL, end - (sg.first_tile + sg.lt)));
+  sg.next = end;
+  return sg;
+}
+
 // Tiles of a sequence at position pos in this launch (0 when the position is
 // invalid; *ok says whether it was valid). With append, the new token must be the last
 // local slot (always true for plain decode, where the local range is the whole
@@ -178,6 +210,12 @@ __device__ __forceinline__ int pair_tiles(const DecodeParams& p, int pos, bool* 
                                  pos - p.slot_offset == hi));
   if (ok_out) *ok_out = ok;
   return ok && hi >= lo ? (hi - lo + kTile) / kTile : 0;
+}
+
+// Partition units of a sequence with `tiles` tiles per kv head (none if empty).
+template <int D>
+__device__ __forceinline__ int pair_units(int tiles, int Hk) {
+  return tiles > 0 ? (tiles + Units<D>::kSetup) * Hk : 0;
 }
 
 // Inclusive scan of prefix[1..batch] by warp 0 (prefix[0] = 0).
@@ -215,10 +253,8 @@ __device__ __forceinline__ void prefetch_first_tiles(const DecodeParams& p, cons
   int b = 0, done = 0;
   for (long long g = tb; g < te && done < kPrefetchTiles;) {
     while (prefix[b + 1] <= g) ++b;
-    const int tiles = (prefix[b + 1] - prefix[b]) / Hk;
-    const int off = static_cast<int>(g - prefix[b]);
-    const int kvh = off / tiles, lt = off - kvh * tiles;
-    const int n = static_cast<int>(min(te - g, static_cast<long long>(tiles - lt)));
+    const Seg sg = seg_at(prefix, b, Hk, Units<D>::kSetup, g, te);
+    const int kvh = sg.kvh, lt = sg.lt, n = sg.n;
     int lo, hi;
     seq_range(p.a, p.positions[b], p.slot_offset, p.local_tokens, &lo, &hi);
     for (int j = lt; j < lt + n && done < kPrefetchTiles; ++j, ++done) {
@@ -226,7 +262,7 @@ __device__ __forceinline__ void prefetch_first_tiles(const DecodeParams& p, cons
       tma_prefetch_l2_3d(&p.tmap_k, 0, y, z);
       tma_prefetch_l2_3d(&p.tmap_v, 0, y, z);
     }
-    g += n;
+    g = sg.next;
   }
 }
 
@@ -245,9 +281,7 @@ __device__ __forceinline__ void prefetch_first_rows(const DecodeParams& p, const
   const LayerArgs& a = p.a;
   int b = 0;
   while (prefix[b + 1] <= tb) ++b;
-  const int tiles = (prefix[b + 1] - prefix[b]) / a.Hk;
-  const int off = static_cast<int>(tb - prefix[b]);
-  const int kvh = off / tiles;
+  const int kvh = seg_at(prefix, b, a.Hk, Units<D>::kSetup, tb, te).kvh;
   const char* row = static_cast<const char*>(p.qkv) + static_cast<size_t>(b) * (a.Hq + 2 * a.Hk) * D * sizeof(IO);
   constexpr int kRowLines = D * sizeof(IO) / 128;  // 128-byte lines per head row (D * sizeof(IO) >= 128)
   const int q_lines = a.G * kRowLines;
@@ -294,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
   // tiles into L2 (a prefetch cannot return stale data: L2 is where writes
   // land); after the wait the positions are read again and the partition is
   // rebuilt only if one of them changed.
-  for (int b = tid; b < p.batch; b += kThreads) prefix[b + 1] = pair_tiles(p, p.positions[b], nullptr) * Hk;
+  for (int b = tid; b < p.batch; b += kThreads) prefix[b + 1] = pair_units<D>(pair_tiles(p, p.positions[b], nullptr), Hk);
   if (tid == 0) prefix[0] = 0;
   __syncthreads();
   scan_prefix(prefix, p.batch, warp, lane);
@@ -322,10 +356,10 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     spos[b] = pos;
     const int tiles = pair_tiles(p, pos, &ok);
     if (!ok && cta == 0) report_error(a.error, TLA_ERR_POSITION);
-    changed |= tiles * Hk != prefix[b + 1] - prefix[b];
+    changed |= pair_units<D>(tiles, Hk) != prefix[b + 1] - prefix[b];
   }
   if (__syncthreads_or(changed)) {
-    for (int b = tid; b < p.batch; b += kThreads) prefix[b + 1] = pair_tiles(p, spos[b], nullptr) * Hk;
+    for (int b = tid; b < p.batch; b += kThreads) prefix[b + 1] = pair_units<D>(pair_tiles(p, spos[b], nullptr), Hk);
     __syncthreads();
     scan_prefix(prefix, p.batch, warp, lane);
     __syncthreads();
@@ -360,10 +394,8 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       int b = 0;
       for (long long g = tb; g < te;) {
         while (prefix[b + 1] <= g) ++b;
-        const int tiles = (prefix[b + 1] - prefix[b]) / Hk;
-        const int off = static_cast<int>(g - prefix[b]);
-        const int kvh = off / tiles, lt = off - kvh * tiles;
-        const int n = static_cast<int>(min(te - g, static_cast<long long>(tiles - lt)));
+        const Seg sg = seg_at(prefix, b, Hk, Units<D>::kSetup, g, te);
+        const int kvh = sg.kvh, lt = sg.lt, n = sg.n;
         int lo, hi;
         seq_range(a, spos[b], p.slot_offset, p.local_tokens, &lo, &hi);
         if (it == 0) DTRACE(13);
@@ -381,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
           tma_load_3d(kst + C::kTileBytes, &p.tmap_v, &full[s], 0, y * C::kHalves, z);
           if (it == 0) DTRACE(5);
         }
-        g += n;
+        g = sg.next;
       }
       // Do not leave the CTA with copies in flight: the last stages' loads
       // have landed once their full barriers completed.
@@ -409,10 +441,12 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
 
   for (long long g = tb; g < te;) {
     while (prefix[b + 1] <= g) ++b;
-    const int tiles = (prefix[b + 1] - prefix[b]) / Hk;
-    const int off = static_cast<int>(g - prefix[b]);
-    const int kvh = off / tiles, lt = off - kvh * tiles;
-    const int n = static_cast<int>(min(te - g, static_cast<long long>(tiles - lt)));
+    const Seg sg = seg_at(prefix, b, Hk, Units<D>::kSetup, g, te);
+    const int tiles = sg.tiles, kvh = sg.kvh, lt = sg.lt, n = sg.n;
+    if (n == 0) {  // this CTA ends inside the pair's set-up units
+      g = sg.next;
+      continue;
+    }
     const int pos = spos[b];
     int lo, hi;
     seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
@@ -727,14 +761,17 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         // are independent, so the maxima and sums are block reductions and
         // the output rows loop over segments without serial dependences.
         __threadfence();
-        const long long pb = prefix[b] + static_cast<long long>(kvh) * tiles;
-        const int c0 = cta_of(pb, total, grid), c1 = cta_of(pb + tiles - 1, total, grid);
+        const long long start = prefix[b] + static_cast<long long>(kvh) * (tiles + Units<D>::kSetup);
+        const long long first_tile = start + Units<D>::kSetup;
+        const int c0 = cta_of(first_tile, total, grid), c1 = cta_of(first_tile + tiles - 1, total, grid);
         // Slot of each contributing CTA (-1: empty range), computed once; qf is
-        // free here and holds 16*D ints (the host keeps grid <= 16*D).
+        // free here and holds 16*D ints (the host keeps grid <= 16*D). A CTA
+        // whose range starts at or after the pair's first unit holds the pair
+        // as its first segment (slot 0), otherwise as its last (slot 1).
         int* slot_of = reinterpret_cast<int*>(qf);
         for (int c = c0 + tid; c <= c1; c += 128) {
           const long long cb = cta_begin(c, total, grid);
-          slot_of[c - c0] = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
+          slot_of[c - c0] = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= start ? 0 : 1);
         }
         named_barrier_sync(1, 128);
         auto seg = [&](int c) -> const float* {  // this pair's triple block in CTA c's scratch, or null
@@ -817,7 +854,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       }
     }
     named_barrier_sync(1, 128);  // red / q_s / flags reuse by the next segment
-    g += n;
+    g = min(te, prefix[b] + static_cast<long long>(kvh) * (tiles + Units<D>::kSetup) + Units<D>::kSetup + tiles);
   }
   if (tid == 0) DTRACE(4);
 }
@@ -864,7 +901,7 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
     const bool ok = pos >= 0 && (p.partial_out != nullptr || pos < a.max_tokens) &&
                     (!p.append || (pos - p.slot_offset >= 0 && pos - p.slot_offset < a.max_tokens &&
                                    pos - p.slot_offset == hi));
-    prefix[bb + 1] = (ok && hi >= lo) ? static_cast<long long>((hi - lo + kTile) / kTile) * Hk : 0;
+    prefix[bb + 1] = pair_units<D>((ok && hi >= lo) ? (hi - lo + kTile) / kTile : 0, Hk);
   }
   __syncthreads();
   if (tid == 0) {
@@ -877,17 +914,17 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
   }
   __syncthreads();
   const long long total = prefix[p.batch];
-  const int tiles = static_cast<int>((prefix[b + 1] - prefix[b]) / Hk);
-  if (tiles == 0) return;
-  const long long pb = prefix[b] + static_cast<long long>(kvh) * tiles;
-  const int c0 = cta_of(pb, total, grid), c1 = cta_of(pb + tiles - 1, total, grid);
+  if (prefix[b + 1] == prefix[b]) return;  // no tiles
+  const Seg sg = seg_at(prefix, b, Hk, Units<D>::kSetup, prefix[b] + (prefix[b + 1] - prefix[b]) / Hk * kvh, total);
+  const int tiles = sg.tiles;
+  const int c0 = cta_of(sg.first_tile, total, grid), c1 = cta_of(sg.first_tile + tiles - 1, total, grid);
   if (c0 == c1) return;  // one CTA held the whole pair
   const int S = c1 - c0 + 1;
   // the segment table (computed before the decode kernel has finished)
   for (int k = tid; k < S; k += NT) {
     const int c = c0 + k;
     const long long cb = cta_begin(c, total, grid);
-    seg_slot[k] = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
+    seg_slot[k] = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= sg.start ? 0 : 1);
   }
   __syncthreads();
   griddep_wait();  // the decode kernel's segments are complete and visible
@@ -1022,7 +1059,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_exchange_kernel(const __
     seq_range(a, pos, p.slot_offset, p.local_tokens, &lo, &hi);
     const bool ok = pos >= 0 && (!p.append || (pos - p.slot_offset >= 0 && pos - p.slot_offset < a.max_tokens &&
                                                 pos - p.slot_offset == hi));
-    prefix[bb + 1] = (ok && hi >= lo) ? static_cast<long long>((hi - lo + kTile) / kTile) * Hk : 0;
+    prefix[bb + 1] = pair_units<D>((ok && hi >= lo) ? (hi - lo + kTile) / kTile : 0, Hk);
   }
   __syncthreads();
   if (tid == 0) {
@@ -1040,9 +1077,13 @@ __global__ void __launch_bounds__(kMergeThreads) decode_exchange_kernel(const __
   const int rows = p.batch * Hq;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const int b = row / Hq, h = row - b * Hq, kvh = h / G, r = h - kvh * G;
-    const int tiles = static_cast<int>((prefix[b + 1] - prefix[b]) / Hk);
-    const long long pb = prefix[b] + static_cast<long long>(kvh) * tiles;
-    const int c0 = tiles ? cta_of(pb, total, grid) : 0, c1 = tiles ? cta_of(pb + tiles - 1, total, grid) : 0;
+    const bool empty = prefix[b + 1] == prefix[b];
+    Seg sg{};
+    if (!empty)
+      sg = seg_at(prefix, b, Hk, Units<D>::kSetup, prefix[b] + (prefix[b + 1] - prefix[b]) / Hk * kvh, total);
+    const int tiles = empty ? 0 : sg.tiles;
+    const int c0 = tiles ? cta_of(sg.first_tile, total, grid) : 0;
+    const int c1 = tiles ? cta_of(sg.first_tile + tiles - 1, total, grid) : 0;
     if (tiles == 0 || c0 == c1) {  // written by the decode kernel (empty pair: m = -inf)
       for (int e = tid; e < W; e += kMergeThreads) trip[e] = __ldcg(p.partial_out + static_cast<size_t>(row) * W + e);
     } else {
@@ -1051,7 +1092,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_exchange_kernel(const __
       for (int k = tid; k < S; k += kMergeThreads) {
         const int c = c0 + k;
         const long long cb = cta_begin(c, total, grid);
-        const int sl = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= pb ? 0 : 1);
+        const int sl = cta_begin(c + 1, total, grid) == cb ? -1 : c * 2 + (cb >= sg.start ? 0 : 1);
         seg_slot[k] = sl;
         float mk = -INFINITY, lk = 0.f;
         if (sl >= 0) {
