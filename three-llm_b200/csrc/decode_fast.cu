@@ -166,12 +166,14 @@ __device__ __forceinline__ int cta_of(long long g, long long total, int grid) {
 }
 
 // The stream-K split is over partition units: every (sequence, kv head) pair
-// with tiles takes kSetupUnits units before its tiles, so a CTA that starts
-// several pairs (each with a query set-up and an epilogue, measured at about
-// two 64-token tiles of streaming at head_dim 128) gets fewer tiles.
+// with tiles takes kSetup units before its tiles, so a CTA that starts
+// several pairs (each with a query set-up and an epilogue) gets fewer tiles.
+// The weights are measured optima (B200, configs 2 and 4 and their head
+// shards): a pair's set-up and epilogue cost about as much as streaming
+// twelve 64-token tiles at head_dim 64, four at head_dim 128.
 template <int D>
 struct Units {
-  static constexpr int kSetup = D == 64 ? 4 : 2;
+  static constexpr int kSetup = D == 64 ? 12 : 4;
 };
 
 // The pair holding unit g of sequence b (prefix[b] <= g < prefix[b + 1]) and
