@@ -889,6 +889,12 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
   __shared__ int seg_slot[kMaxGrid];   // scratch slot of segment k, -1 if none
   __shared__ float red[2][kWarps];
   __shared__ float rows_s[kWarps][kCols];
+  // The next kernel may launch as soon as every block of this one is
+  // resident: it can only start its own prologue (its griddepcontrol.wait
+  // waits for this grid to complete), and these blocks need no more resources
+  // to finish, so its CTAs can take the SMs that the decode kernel frees and
+  // start their L2 prefetches early.
+  griddep_launch_dependents();
   const LayerArgs& a = p.a;
   const int G = a.G, Hk = a.Hk;
   const int slice = static_cast<int>(blockIdx.x) % kSlices, row_id = static_cast<int>(blockIdx.x) / kSlices;
@@ -930,7 +936,6 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
   }
   __syncthreads();
   griddep_wait();  // the decode kernel's segments are complete and visible
-  griddep_launch_dependents();
   // One pass: warp w folds segments w, w + NT / 32, ... with a running
   // maximum (the online softmax across segments), loading the triples of kB
   // segments at once; then the warps' partial triples are combined.
