@@ -118,7 +118,11 @@ __device__ __forceinline__ float ex2_poly(float x) {
 
 #ifdef TLA_PREFILL_TRACE
 // Optional pipeline trace (builds with -DTLA_PREFILL_TRACE only): SM clock of
-// each event of block 0, [tile][event]; read with tla_debug_prefill_trace.
+// each event of block 0's first 64 global steps, [step][event]; read with
+// tla_debug_prefill_trace. Softmax (warp 0 unless noted): [0] S(g) complete,
+// [1] P V(g-2) complete, [2] S(g) loaded, [3 + w] warp w's P(g) stored. MMA
+// issuer: [8]/[9] S(g) issue start/end, [12]/[13] before/after the V(g)
+// wait, [10]/[11] P V(g) issue start/end.
 __device__ unsigned long long g_prefill_trace[64][16];
 #define PTRACE(ev, n) \
   do { \
@@ -398,7 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         const int st = gp % C::kST;
         if (np == 0 && kp >= C::kNO)  // the epilogue of item kp - NO has read this O buffer
           spin(&o_free[kp % C::kNO], ((kp / C::kNO) - 1) & 1);
+        PTRACE(12, gp);
         spin(&v_full[st], (gp / C::kST) & 1);
+        PTRACE(13, gp);
         // the softmax step is usually still running: sleep on the barrier
         // instead of spinning, which would take issue slots from the softmax
         // warp on this sub-partition
@@ -456,12 +462,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         const int j = g % NS;
         const uint32_t buf = lane_addr + 128 * j;
         wait(&s_full[j], (g / NS) & 1);
+        if (tid == 0) PTRACE(0, g);
         if (g >= 2) wait(&o_done[g & 1], ((g - 2) >> 1) & 1);  // P V(g-2): keeps o_done within one phase
         __syncwarp();
         tc_fence_after();
+        if (tid == 0) PTRACE(1, g);
         uint32_t sv[128];
         tmem_ld64x(buf, *reinterpret_cast<uint32_t(*)[64]>(&sv[0]));
         tmem_ld64x(buf + 64, *reinterpret_cast<uint32_t(*)[64]>(&sv[64]));
+        if (tid == 0) PTRACE(2, g);
         release_p();  // the previous step's P (its P V may now be issued)
         const int tok0 = (w.j0 + n) * kT;
         const bool masked = tok0 + kT - 1 > pr || tok0 < first_r;
@@ -521,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           tmem_st32(buf + 32 * c, pk);
         }
         l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+        if (lane == 0) PTRACE(3 + warp, g);
         pend_j = j;
       }
       release_p();
