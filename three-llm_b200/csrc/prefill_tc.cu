@@ -195,8 +195,13 @@ __device__ __forceinline__ void tmem_ld64x(uint32_t taddr, uint32_t (&r)[64]) {
 // P V finished), so P stays <= 256 in fp16.
 // P V(g) completion is signalled on o_done[g & 1]. A softmax thread can be up
 // to two P V steps behind the issuer, which one barrier's phase parity cannot
-// tell apart; with two barriers, and the softmax waiting for P V(g-2) at every
-// step g, each barrier is at most one phase from any phase a thread waits for.
+// tell apart; with two barriers each barrier is at most one phase from any
+// phase a thread waits for: S(g) is issued after P V(g - NS) (NS <= 3) and its
+// commit tracks every earlier MMA, so once S(g) is complete P V(g-3) is too,
+// and the rescale at step g (waiting for P V(g-1), whose barrier last
+// completed for P V(g-3)) and the item epilogue (P V(g-2), then P V(g-1)) wait
+// on a barrier at most one phase behind. The softmax therefore waits for O
+// only when it reads it.
 // TMEM columns: S/P buffer j at 128 j (j < NS), O buffer i at 128 NS + D i (i < NO).
 constexpr int kThreads = 192;  // warps 0-3: softmax, 4: TMA, 5: MMA
 constexpr int kMmaWarp = 5, kTmaWarp = 4;
@@ -254,6 +259,7 @@ template <int D, typename OUT>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
   using C = PCfg<D>;
   constexpr int kT = 128, NS = C::kNS;
+  static_assert(NS <= 3, "the o_done parity argument needs S(g) to be issued after P V(g-3) or later");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
@@ -463,7 +469,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         const uint32_t buf = lane_addr + 128 * j;
         wait(&s_full[j], (g / NS) & 1);
         if (tid == 0) PTRACE(0, g);
-        if (g >= 2) wait(&o_done[g & 1], ((g - 2) >> 1) & 1);  // P V(g-2): keeps o_done within one phase
         __syncwarp();
         tc_fence_after();
         if (tid == 0) PTRACE(1, g);
@@ -535,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       }
       release_p();
       // ---- item epilogue: normalise and store this row's outputs, then free O
-      // the last step waited for P V(g-3); now P V(g-2) and P V(g-1)
+      // S(g-1) complete implies P V(g-4); now P V(g-2), then P V(g-1)
       if (g >= 2) wait(&o_done[g & 1], ((g - 2) >> 1) & 1);
       wait(&o_done[(g - 1) & 1], ((g - 1) >> 1) & 1);
       __syncwarp();
