@@ -470,10 +470,10 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         qv[u] = i < G * D ? to_f32(__ldg(row + kvh * G * D + i)) : 0.f;
       }
       float kv0 = 0.f, kv1 = 0.f, kv2 = 0.f, kv3 = 0.f;  // the new K/V: D <= 256 values each
-      if (has_new) {
+      if (has_new && (D >= 128 || tid < D)) {  // (at D = 64 a wider read would run past the last V row)
         kv0 = to_f32(__ldg(row + (Hq + kvh) * D + tid));
         kv1 = to_f32(__ldg(row + (Hq + Hk + kvh) * D + tid));
-        if (D > 128) {
+        if (D > 128 && 128 + tid < D) {
           kv2 = to_f32(__ldg(row + (Hq + kvh) * D + 128 + tid));
           kv3 = to_f32(__ldg(row + (Hq + Hk + kvh) * D + 128 + tid));
         }
