@@ -53,6 +53,14 @@ WORKLOAD_LABELS = {
     "prefill_05b": "prefill_05b (config 3)",
 }
 PREFILL_05B = dict(Hq=14, Hk=2, D=64, S=2048, B=4, T=4096, theta=1e6)
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu
+# --set full capture of each kernel (the commands are in profiles/). The decode
+# capture is config 2 at batch 16 (134.47 + 3.78 MB for 16 sequences); the
+# traffic grows with the sequences a launch covers, so a launch of B sequences
+# is B times the per-sequence figure. The prefill capture is the full config-3
+# call (18.93 MB read, nothing written back to DRAM).
+NCU_DECODE_1B_BYTES_PER_SEQ = (134.466816e6 + 3.778304e6) / 16
+NCU_PREFILL_05B_BYTES = 18.933504e6  # read; 0 bytes written
 
 
 def peaks():
@@ -166,6 +174,7 @@ class Decode1B:
         self.outs = torch.empty(L, B, Hq * D, dtype=torch.float16, device=device)
         self.bytes_per_step = L * B * decode_seq_bytes(T + 1, Hq, Hk, D)
         self.bytes_per_launch = B * decode_seq_bytes(T + 1, Hq, Hk, D)
+        self.traffic_per_launch = B * NCU_DECODE_1B_BYTES_PER_SEQ
         self.tokens_per_step = B
         self.launches_per_step = L
         self.kernel = "decode_fast_kernel<64,half>"
@@ -587,7 +596,9 @@ def main():
                               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
                               "data": "synthetic", "config": {"workload": "prefill_05b (config 3)"},
                               "roofline": {"bound": "tensor", "achieved": round(pre["tflops"], 2), "peak": tc,
-                                           "unit": "TFLOP/s", "frac": round(pre["tflops"] / tc, 4), "traffic": None,
+                                           "unit": "TFLOP/s", "frac": round(pre["tflops"] / tc, 4),
+                                           "traffic": round(NCU_PREFILL_05B_BYTES),
+                                           "traffic_unit": "DRAM bytes per attention launch (ncu)",
                                            "peak_source": src}, "gpu_launches": pre["launches"]}), flush=True)
         if world > 1:
             torch.distributed.barrier()
@@ -614,7 +625,10 @@ def main():
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic (seeded N(0,1) fp16 cache and qkv)",
             "config": wl.config, "tok_s": round(tokens / (ms * 1e-3), 1), "hbm_frac": round(gbs / world / hbm, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "traffic": None, "kernel": wl.kernel,
+                         "frac": round(achieved / hbm, 4),
+                         "traffic": (round(wl.traffic_per_launch) if getattr(wl, "traffic_per_launch", None)
+                                     else None),
+                         "traffic_unit": "DRAM bytes per launch (ncu, scaled by sequences)", "kernel": wl.kernel,
                          "peak_source": src, "launch_ms": round(per_launch, 5)},
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": wl.h2d,
                     "d2h_bytes_per_step": wl.d2h, "ms_per_step": round(e2e_ms / args.steps, 4)},
