@@ -203,8 +203,8 @@ __device__ __forceinline__ void tmem_ld64x(uint32_t taddr, uint32_t (&r)[64]) {
 // on a barrier at most one phase behind. The softmax therefore waits for O
 // only when it reads it.
 // TMEM columns: S/P buffer j at 128 j (j < NS), O buffer i at 128 NS + D i (i < NO).
-constexpr int kThreads = 192;  // warps 0-3: softmax, 4: TMA, 5: MMA
-constexpr int kMmaWarp = 5, kTmaWarp = 4;
+constexpr int kThreads = 224;  // warps 0-3: softmax, 4: TMA, 5: P V issuer (and TMEM owner), 6: S issuer
+constexpr int kMmaWarp = 5, kTmaWarp = 4, kSWarp = 6;
 
 template <int D>
 struct PCfg {
@@ -356,8 +356,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       for (int q = max(0, g - C::kST); q < g; ++q)  // no copies in flight at exit
         wait(&full[q % C::kST], (q / C::kST) & 1);
     }
-  } else if (warp == kMmaWarp) {
-    // ================================================================ MMA issuer
+  } else if (warp == kMmaWarp || warp == kSWarp) {
+    // ================================================================ MMA issuers
+    // Two issuing threads, so that one's waits, commits and bookkeeping
+    // overlap the other's MMAs: warp kSWarp issues every S(g) (S(g) for
+    // g >= NS once P V(g - NS) has completed, i.e. has read P(g - NS) from
+    // the buffer S(g) overwrites), warp kMmaWarp every P V(g) once the
+    // softmax has stored P(g). A tcgen05.commit tracks the issuing thread's
+    // own MMAs, and each barrier has a single committing thread.
     if (lane == 0) {
       constexpr uint32_t kIdS = idesc_f16(128, kT, false);
       constexpr uint32_t kIdO = idesc_f16(128, D, true);
@@ -369,72 +375,74 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const uint64_t dq = sdesc(smem_u32(smem + C::kQ), 16, 1024);
       const uint64_t dk = sdesc(smem_u32(smem + C::kK), 16, 1024);
       const uint64_t dv = sdesc(smem_u32(smem + C::kV), C::kBox, 1024);
-      // S cursor (item ks, local step ns, global step gs) runs NS steps ahead
-      // of the P V cursor (kp, np, gp).
-      int ks = 0, ns = 0, gs = 0, its = prefill_item_of(0, num_items);
-      int Ns = its >= 0 ? prefill_item(p, its).N : 0;
-      auto issue_s = [&]() -> bool {  // S(gs) = Q K(gs)^T into buffer gs % NS; false when no step is left
-        if (its < 0) return false;
-        if (ns == 0) spin(&q_full[ks % C::kNQ], (ks / C::kNQ) & 1);
-        const int st = gs % C::kST;
-        spin(&k_full[st], (gs / C::kST) & 1);
-        PTRACE(8, gs);
-        const uint64_t qb = dq + static_cast<uint64_t>((ks % C::kNQ) * (C::kTile >> 4));
-        const uint64_t kb = dk + static_cast<uint64_t>(st * (C::kTile >> 4));
-        const uint32_t d = tmem + 128 * (gs % NS);
-        if (!*abort_flag) {
+      if (warp == kSWarp) {
+        // S cursor: item ks, local step ns, global step gs
+        int ks = 0, ns = 0, gs = 0, its = prefill_item_of(0, num_items);
+        int Ns = its >= 0 ? prefill_item(p, its).N : 0;
+        while (its >= 0) {  // S(gs) = Q K(gs)^T into buffer gs % NS
+          // P V(gs - NS) has read P from this buffer (its barrier last
+          // completed for P V(gs - NS - 2), which the previous wait covers)
+          if (gs >= NS) wait(&o_done[(gs - NS) & 1], ((gs - NS) >> 1) & 1);
+          if (ns == 0) spin(&q_full[ks % C::kNQ], (ks / C::kNQ) & 1);
+          const int st = gs % C::kST;
+          spin(&k_full[st], (gs / C::kST) & 1);
+          PTRACE(8, gs);
+          const uint64_t qb = dq + static_cast<uint64_t>((ks % C::kNQ) * (C::kTile >> 4));
+          const uint64_t kb = dk + static_cast<uint64_t>(st * (C::kTile >> 4));
+          const uint32_t d = tmem + 128 * (gs % NS);
+          if (!*abort_flag) {
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = ((kk >> 2) * C::kBox + (kk & 3) * 32) >> 4;
-            mma_f16(d, qb + off, kb + off, kIdS, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = ((kk >> 2) * C::kBox + (kk & 3) * 32) >> 4;
+              mma_f16(d, qb + off, kb + off, kIdS, kk > 0 ? 1u : 0u);
+            }
+          }
+          mma_commit(&s_full[gs % NS]);
+          mma_commit(&k_empty[st]);
+          PTRACE(9, gs);
+          ++gs;
+          if (++ns == Ns) {  // this item's last S: its Q tile is free
+            mma_commit(&q_empty[ks % C::kNQ]);
+            ns = 0;
+            its = prefill_item_of(++ks, num_items);
+            Ns = its >= 0 ? prefill_item(p, its).N : 0;
           }
         }
-        mma_commit(&s_full[gs % NS]);
-        mma_commit(&k_empty[st]);
-        PTRACE(9, gs);
-        ++gs;
-        if (++ns == Ns) {  // this item's last S: its Q tile is free
-          mma_commit(&q_empty[ks % C::kNQ]);
-          ns = 0;
-          its = prefill_item_of(++ks, num_items);
-          Ns = its >= 0 ? prefill_item(p, its).N : 0;
-        }
-        return true;
-      };
-      for (int i = 0; i < NS; ++i) issue_s();
-      int kp = 0, np = 0, gp = 0, itp = prefill_item_of(0, num_items);
-      int Np = itp >= 0 ? prefill_item(p, itp).N : 0;
-      while (itp >= 0) {  // O(item) += P(gp) V(gp) once the softmax step is done, then S(gp + NS)
-        const int st = gp % C::kST;
-        if (np == 0 && kp >= C::kNO)  // the epilogue of item kp - NO has read this O buffer
-          spin(&o_free[kp % C::kNO], ((kp / C::kNO) - 1) & 1);
-        PTRACE(12, gp);
-        spin(&v_full[st], (gp / C::kST) & 1);
-        PTRACE(13, gp);
-        // the softmax step is usually still running: sleep on the barrier
-        // instead of spinning, which would take issue slots from the softmax
-        // warp on this sub-partition
-        wait(&p_full[gp % NS], (gp / NS) & 1);
-        tc_fence_after();
-        PTRACE(10, gp);
-        const uint64_t vb = dv + static_cast<uint64_t>(st * (C::kTile >> 4));
-        const uint32_t a = tmem + 128 * (gp % NS);
-        const uint32_t o = tmem + C::kO + D * (kp % C::kNO);
-        if (!*abort_flag) {
+      } else {
+        // P V cursor: item kp, local step np, global step gp
+        int kp = 0, np = 0, gp = 0, itp = prefill_item_of(0, num_items);
+        int Np = itp >= 0 ? prefill_item(p, itp).N : 0;
+        while (itp >= 0) {  // O(item) += P(gp) V(gp) once the softmax step is done
+          const int st = gp % C::kST;
+          if (np == 0 && kp >= C::kNO)  // the epilogue of item kp - NO has read this O buffer
+            spin(&o_free[kp % C::kNO], ((kp / C::kNO) - 1) & 1);
+          PTRACE(12, gp);
+          spin(&v_full[st], (gp / C::kST) & 1);
+          PTRACE(13, gp);
+          // the softmax step is usually still running: sleep on the barrier
+          // instead of spinning, which would take issue slots from the softmax
+          // warp on this sub-partition
+          wait(&p_full[gp % NS], (gp / NS) & 1);
+          tc_fence_after();
+          PTRACE(10, gp);
+          const uint64_t vb = dv + static_cast<uint64_t>(st * (C::kTile >> 4));
+          const uint32_t a = tmem + 128 * (gp % NS);
+          const uint32_t o = tmem + C::kO + D * (kp % C::kNO);
+          if (!*abort_flag) {
 #pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk)
-            mma_f16_ts(o, a + kk * 8, vb + 128 * kk, kIdO, (np > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < kT / 16; ++kk)
+              mma_f16_ts(o, a + kk * 8, vb + 128 * kk, kIdO, (np > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&o_done[gp & 1]);
+          mma_commit(&v_empty[st]);
+          PTRACE(11, gp);
+          ++gp;
+          if (++np == Np) {
+            np = 0;
+            itp = prefill_item_of(++kp, num_items);
+            Np = itp >= 0 ? prefill_item(p, itp).N : 0;
+          }
         }
-        mma_commit(&o_done[gp & 1]);
-        mma_commit(&v_empty[st]);
-        PTRACE(11, gp);
-        ++gp;
-        if (++np == Np) {
-          np = 0;
-          itp = prefill_item_of(++kp, num_items);
-          Np = itp >= 0 ? prefill_item(p, itp).N : 0;
-        }
-        issue_s();
       }
     }
   } else {
