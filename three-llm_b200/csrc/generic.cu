@@ -362,6 +362,13 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(LayerArgs a, cons
   }
 }
 
+#ifndef TLA_ROPE_MIN_BLOCKS
+#define TLA_ROPE_MIN_BLOCKS 1  // resident 128-thread blocks per SM the register budget must allow
+#endif
+#ifndef TLA_ROPE_LOADS
+#define TLA_ROPE_LOADS 8
+#endif
+
 // fp16 rows, head_dim 64 or 128: a warp per token, each lane owns 16 bytes
 // (8 dims) of a head, so one warp-wide load covers 32 / (D / 8) heads and the
 // whole qkv row is in flight in a few loads; the rotate-half partner is
@@ -369,12 +376,12 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(LayerArgs a, cons
 // lane group), RMS norms reduce over the group, and cos/sin are computed once
 // per token (lane k: pairs k and k + 32) and gathered by shuffles.
 template <int D>
-__global__ void __launch_bounds__(128) rope_rows_kernel(LayerArgs a, const __half* __restrict__ qkv,
+__global__ void __launch_bounds__(128, TLA_ROPE_MIN_BLOCKS) rope_rows_kernel(LayerArgs a, const __half* __restrict__ qkv,
                                                         const int32_t* __restrict__ start, int seq_len, int tokens,
                                                         __half* __restrict__ qscr) {
   constexpr int L = D / 8;     // lanes per head
   constexpr int HPW = 32 / L;  // heads per warp-wide load
-  constexpr int kLoads = 8;    // warp-wide loads in flight per round
+  constexpr int kLoads = TLA_ROPE_LOADS;  // warp-wide loads in flight per round
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int ti = blockIdx.x * 4 + (threadIdx.x >> 5);

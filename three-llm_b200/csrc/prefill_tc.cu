@@ -134,6 +134,25 @@ __device__ unsigned long long g_prefill_trace[64][16];
   } while (0)
 #endif
 
+#ifndef TLA_PREFILL_HELPER_NAP
+#define TLA_PREFILL_HELPER_NAP 0  // > 0: the TMA and MMA warps poll with this __nanosleep (ns) between tests
+#endif
+
+// Bounded poll with a sleep of `ns` between tests (for the helper warps, which
+// share sub-partitions with the softmax warps).
+__device__ __forceinline__ bool nap_wait(uint64_t* bar, uint32_t parity, int* err, int ns) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (int i = 0;; ++i) {
+    __nanosleep(ns);
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 63) == 63 && globaltimer() - t0 > kWaitLimitNs) {
+      report_error(err, TLA_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 #ifndef TLA_PREFILL_POLY_EVERY
 #define TLA_PREFILL_POLY_EVERY 0  // every n-th pair of exponentials goes to the FMA pipe (0: none)
 #endif
@@ -175,13 +194,14 @@ __device__ __forceinline__ void tmem_ld64x(uint32_t taddr, uint32_t (&r)[64]) {
 // and the barriers flow from one item into the next without a drain, and the
 // next item's Q load and first S MMAs overlap the current item's epilogue.
 //
-// The tcgen05 pipe runs one MMA at a time and the issuing thread waits for
-// each to be accepted, so the issuer's instruction stream is the tensor
-// timeline. NS TMEM S buffers let it run S NS steps ahead of P V: the issue
-// order is S(0) .. S(NS-1) PV(0) S(NS) PV(1) ..., so S(g) is long finished
-// when the softmax warpgroup reaches step g, and the issuer only ever waits
-// for a softmax step before its P V. N = 128 for the S MMAs (full rate) and
-// N = head_dim for P V.
+// The tcgen05 pipe runs one MMA at a time and an issuing thread waits for
+// each to be accepted. Two issuing threads share it: one issues every S(g),
+// the other every P V(g), so one's waits, commits and bookkeeping overlap the
+// other's MMAs. NS TMEM S buffers let S run NS steps ahead of P V: S(g) is
+// issued once P V(g - NS) has completed (it read P(g - NS) from the buffer
+// S(g) overwrites), which gives the order S(0) .. S(NS-1) PV(0) S(NS) PV(1)
+// ..., so S(g) is usually finished when the softmax warpgroup reaches step g.
+// N = 128 for the S MMAs (full rate) and N = head_dim for P V.
 // Softmax thread = one query row (TMEM lane), all 128 columns of the step in
 // registers (one pass). P(g) is written as fp16 pairs over the first 64
 // columns of its own S buffer and read from there as the A operand of P V;
@@ -196,12 +216,14 @@ __device__ __forceinline__ void tmem_ld64x(uint32_t taddr, uint32_t (&r)[64]) {
 // P V(g) completion is signalled on o_done[g & 1]. A softmax thread can be up
 // to two P V steps behind the issuer, which one barrier's phase parity cannot
 // tell apart; with two barriers each barrier is at most one phase from any
-// phase a thread waits for: S(g) is issued after P V(g - NS) (NS <= 3) and its
-// commit tracks every earlier MMA, so once S(g) is complete P V(g-3) is too,
-// and the rescale at step g (waiting for P V(g-1), whose barrier last
-// completed for P V(g-3)) and the item epilogue (P V(g-2), then P V(g-1)) wait
-// on a barrier at most one phase behind. The softmax therefore waits for O
-// only when it reads it.
+// phase a thread waits for: S(g) is issued only after P V(g - NS) (NS <= 3)
+// has completed, so once S(g) is complete P V(g-3) is too, and the rescale at
+// step g (waiting for P V(g-1), whose barrier last completed for P V(g-3)) and
+// the item epilogue (P V(g-2), then P V(g-1)) wait on a barrier at most one
+// phase behind. The softmax therefore waits for O only when it reads it.
+// The S issuer's own wait for P V(g - NS) is not overtaken by P V(g-1) on the
+// same barrier: P V(g-1) needs P(g-1), which the softmax releases only after
+// it has loaded S(g), also across items.
 // TMEM columns: S/P buffer j at 128 j (j < NS), O buffer i at 128 NS + D i (i < NO).
 constexpr int kThreads = 224;  // warps 0-3: softmax, 4: TMA, 5: P V issuer (and TMEM owner), 6: S issuer
 constexpr int kMmaWarp = 5, kTmaWarp = 4, kSWarp = 6;
@@ -218,7 +240,12 @@ struct PCfg {
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + kNQ * kTile;
   static constexpr int kV = kK + kST * kTile;
-  static constexpr int kBar = kV + kST * kTile;
+  // per-warp staging of the item epilogue's output rows (32 rows x D x up to 4
+  // bytes), so the global stores cover whole rows; head_dim 64 only (at 128
+  // the K/V stages take the room)
+  static constexpr int kOut = kV + kST * kTile;
+  static constexpr int kOutBytes = D == 64 ? 4 * 32 * D * 4 : 0;
+  static constexpr int kBar = kOut + kOutBytes;
   // q_full, q_empty [2]; k_full, v_full, k_empty, v_empty [kST]; s_full, p_full [kNS]; o_done, o_free [2]
   static constexpr int kNumBars = 4 + 4 * kST + 2 * kNS + 4;
   static constexpr int kSmem = kBar + kNumBars * 8 + 16 + 1024;
@@ -313,6 +340,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     if (*abort_flag) return;
     if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
   };
+  auto hwait = [&](uint64_t* bar, uint32_t parity) {  // the TMA and MMA warps' waits
+#if TLA_PREFILL_HELPER_NAP > 0
+    if (*abort_flag) return;
+    if (!nap_wait(bar, parity, p.error, TLA_PREFILL_HELPER_NAP)) *abort_flag = 1;
+#else
+    wait(bar, parity);
+#endif
+  };
 
   if (warp == kTmaWarp) {
     // ================================================================ TMA producer
@@ -333,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         const int z = w.b * p.Hk + w.h / p.G;
         if (lane == 0) {
           const int qi = k % C::kNQ;
-          wait(&q_empty[qi], ((k / C::kNQ) & 1) ^ 1);
+          hwait(&q_empty[qi], ((k / C::kNQ) & 1) ^ 1);
           if (!*abort_flag) {
             mbar_arrive_expect_tx(&q_full[qi], C::kTile);
 #pragma unroll
@@ -344,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
         for (int n = 0; n < w.N; ++n, ++g) {
           const int st = g % C::kST;
-          wait(&empty[st], ((g / C::kST) & 1) ^ 1);
+          hwait(&empty[st], ((g / C::kST) & 1) ^ 1);
           if (!*abort_flag) {
             mbar_arrive_expect_tx(&full[st], C::kTile);
 #pragma unroll
@@ -354,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
       }
       for (int q = max(0, g - C::kST); q < g; ++q)  // no copies in flight at exit
-        wait(&full[q % C::kST], (q / C::kST) & 1);
+        hwait(&full[q % C::kST], (q / C::kST) & 1);
     }
   } else if (warp == kMmaWarp || warp == kSWarp) {
     // ================================================================ MMA issuers
@@ -368,7 +403,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       constexpr uint32_t kIdS = idesc_f16(128, kT, false);
       constexpr uint32_t kIdO = idesc_f16(128, D, true);
       auto spin = [&](uint64_t* bar, uint32_t parity) {
+#if TLA_PREFILL_HELPER_NAP > 0
+        hwait(bar, parity);
+#else
         if (!*abort_flag && !mbar_spin(bar, parity, p.error)) *abort_flag = 1;
+#endif
       };
       // Descriptors are linear in the start address (bits 0-13 = addr >> 4, no
       // carry below 256 KB), so buffer, stage, box and k-step offsets are plain adds.
@@ -382,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         while (its >= 0) {  // S(gs) = Q K(gs)^T into buffer gs % NS
           // P V(gs - NS) has read P from this buffer (its barrier last
           // completed for P V(gs - NS - 2), which the previous wait covers)
-          if (gs >= NS) wait(&o_done[(gs - NS) & 1], ((gs - NS) >> 1) & 1);
+          if (gs >= NS) hwait(&o_done[(gs - NS) & 1], ((gs - NS) >> 1) & 1);
           if (ns == 0) spin(&q_full[ks % C::kNQ], (ks / C::kNQ) & 1);
           const int st = gs % C::kST;
           spin(&k_full[st], (gs / C::kST) & 1);
@@ -422,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           // the softmax step is usually still running: sleep on the barrier
           // instead of spinning, which would take issue slots from the softmax
           // warp on this sub-partition
-          wait(&p_full[gp % NS], (gp / NS) & 1);
+          hwait(&p_full[gp % NS], (gp / NS) & 1);
           tc_fence_after();
           PTRACE(10, gp);
           const uint64_t vb = dv + static_cast<uint64_t>(st * (C::kTile >> 4));
@@ -464,6 +503,96 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         pend_j = -1;
       }
     };
+    // Item epilogue: normalise and store this row's outputs of item ke (its
+    // last step is global step last), then free its O buffer. It runs inside
+    // the first step of the next item, after that step's P is stored, so the
+    // softmax goes on to the next item's S without waiting for P V(last)
+    // (O is double-buffered by item at head_dim 64; at 128 the next item's
+    // first P V waits for o_free). There, S(last + 1) complete implies
+    // P V(last - 2), and P(last + 1) is not yet released, so the barrier of
+    // P V(last - 1) is one phase from it, and so is that of P V(last) once
+    // P V(last - 1) has completed. After the last item the same waits hold
+    // with S(last) seen (P V(last - 3) complete).
+    auto epilogue = [&](int ke, long long base, int rows, float le, int last) {
+      if (last >= 1) wait(&o_done[(last - 1) & 1], ((last - 1) >> 1) & 1);
+      wait(&o_done[last & 1], (last >> 1) & 1);
+      __syncwarp();
+      tc_fence_after();
+      const uint32_t oe = lane_addr + C::kO + D * (ke % C::kNO);
+      const float inv = le > 0.f ? 1.f / le : 0.f;
+      const size_t row_stride = static_cast<size_t>(p.Hq) * D;  // elements between consecutive tokens
+      OUT* const dst0 = static_cast<OUT*>(p.out) + base;        // row 0 of the item's tile
+      if constexpr (C::kOutBytes > 0) {
+        // Rows go through this warp's shared-memory stage (16-byte chunks
+        // XOR-swizzled by row, so neither side has bank conflicts) and leave
+        // as whole 128- or 256-byte rows: a warp-wide store covers 4 (2) rows
+        // instead of 16 bytes of 32 rows.
+        constexpr int kRowBytes = D * static_cast<int>(sizeof(OUT));
+        constexpr int kChunks = kRowBytes / 16;
+        constexpr int kPer32 = 32 * static_cast<int>(sizeof(OUT)) / 16;  // chunks per 32 values
+        uint8_t* stage = smem + C::kOut + warp * 32 * kRowBytes;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(oe + 32 * c, o);
+#pragma unroll
+          for (int i = 0; i < kPer32; ++i) {
+            uint4 v;
+            if constexpr (sizeof(OUT) == 2) {
+              const float* f = o + 8 * i;
+              v = make_uint4(pack_half2(f[0] * inv, f[1] * inv), pack_half2(f[2] * inv, f[3] * inv),
+                             pack_half2(f[4] * inv, f[5] * inv), pack_half2(f[6] * inv, f[7] * inv));
+            } else {
+              const float* f = o + 4 * i;
+              v = make_uint4(__float_as_uint(f[0] * inv), __float_as_uint(f[1] * inv), __float_as_uint(f[2] * inv),
+                             __float_as_uint(f[3] * inv));
+            }
+            const int q = c * kPer32 + i;
+            *reinterpret_cast<uint4*>(stage + lane * kRowBytes + ((q ^ (lane & 7)) << 4)) = v;
+          }
+        }
+        __syncwarp();
+        constexpr int kRowsPer = 32 / kChunks;
+        const int q = lane % kChunks;
+        const uint8_t* src = stage + (lane / kChunks) * kRowBytes;
+        int row = warp * 32 + lane / kChunks;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(dst0 + row * row_stride) + (q << 4);
+        const size_t dst_step = kRowsPer * row_stride * sizeof(OUT);
+#pragma unroll 1
+        for (int it = 0; it < kChunks; ++it, row += kRowsPer, src += kRowsPer * kRowBytes, dst += dst_step) {
+          const uint4 v = *reinterpret_cast<const uint4*>(src + ((q ^ (row & 7)) << 4));
+          if (row < rows) *reinterpret_cast<uint4*>(dst) = v;
+        }
+        __syncwarp();  // the stage is reused by the next epilogue
+      } else {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(oe + 32 * c, o);
+          if (r < rows) {
+            OUT* dst = dst0 + r * row_stride + 32 * c;
+            if constexpr (sizeof(OUT) == 2) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 8)
+                *reinterpret_cast<uint4*>(dst + i) =
+                    make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv), pack_half2(o[i + 2] * inv, o[i + 3] * inv),
+                               pack_half2(o[i + 4] * inv, o[i + 5] * inv), pack_half2(o[i + 6] * inv, o[i + 7] * inv));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(dst + i) =
+                    make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&o_free[ke % C::kNO]);
+    };
+    int e_k = -1, e_last = 0, e_rows = 0;  // the item whose epilogue is pending, its last step, its rows,
+    long long e_base = 0;                  // the output offset of its first row,
+    float e_l = 0.f;                       // and this row's softmax sum
+    const uint32_t ninf = __float_as_uint(-INFINITY);
     for (int k = 0;; ++k) {
       const int it = prefill_item_of(k, num_items);
       if (it < 0) break;
@@ -487,12 +616,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         release_p();  // the previous step's P (its P V may now be issued)
         const int tok0 = (w.j0 + n) * kT;
         const bool masked = tok0 + kT - 1 > pr || tok0 < first_r;
-        const int lo = first_r - tok0, hi = pr - tok0;  // valid columns [lo, hi]
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (masked) {
+          // valid columns [lo, hi] (lo <= hi: first_r <= pr); one unsigned
+          // compare and a select per column, no branch
+          const int lo = first_r - tok0;
+          const uint32_t span = static_cast<uint32_t>(pr - first_r);
 #pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if (i < lo || i > hi) sv[i] = __float_as_uint(-INFINITY);
+          for (int i = 0; i < 128; ++i) sv[i] = static_cast<uint32_t>(i - lo) <= span ? sv[i] : ninf;
         }
 #pragma unroll
         for (int i = 0; i < 128; i += 8) {  // four independent chains of three-input maxima
@@ -545,39 +676,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
         if (lane == 0) PTRACE(3 + warp, g);
         pend_j = j;
-      }
-      release_p();
-      // ---- item epilogue: normalise and store this row's outputs, then free O
-      // S(g-1) complete implies P V(g-4); now P V(g-2), then P V(g-1)
-      if (g >= 2) wait(&o_done[g & 1], ((g - 2) >> 1) & 1);
-      wait(&o_done[(g - 1) & 1], ((g - 1) >> 1) & 1);
-      __syncwarp();
-      tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      const int row = w.row0 + r;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float o[32];
-        tmem_ld32(o_addr + 32 * c, o);
-        if (row < p.S) {
-          OUT* dst = static_cast<OUT*>(p.out) + ((static_cast<size_t>(w.b) * p.S + row) * p.Hq + w.h) * D + 32 * c;
-          if constexpr (sizeof(OUT) == 2) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8)
-              *reinterpret_cast<uint4*>(dst + i) =
-                  make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv), pack_half2(o[i + 2] * inv, o[i + 3] * inv),
-                             pack_half2(o[i + 4] * inv, o[i + 5] * inv), pack_half2(o[i + 6] * inv, o[i + 7] * inv));
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<float4*>(dst + i) =
-                  make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
-          }
+        if (n == 0 && e_k >= 0) {  // the previous item's epilogue (its last P V is done by now)
+          epilogue(e_k, e_base, e_rows, e_l, e_last);
+          e_k = -1;
         }
       }
-      tc_fence_before();
-      mbar_arrive(&o_free[k % C::kNO]);
+      e_k = k;
+      e_base = ((static_cast<long long>(w.b) * p.S + w.row0) * p.Hq + w.h) * D;
+      e_rows = w.rows;
+      e_l = l_run;
+      e_last = g - 1;
     }
+    release_p();
+    if (e_k >= 0) epilogue(e_k, e_base, e_rows, e_l, e_last);
   }
   tc_fence_before();
   __syncthreads();
