@@ -362,12 +362,15 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(LayerArgs a, cons
   }
 }
 
-#ifndef TLA_ROPE_MIN_BLOCKS
-#define TLA_ROPE_MIN_BLOCKS 1  // resident 128-thread blocks per SM the register budget must allow
-#endif
-#ifndef TLA_ROPE_LOADS
-#define TLA_ROPE_LOADS 8
-#endif
+// Register budget of rope_rows_kernel: at head_dim 64 at least 6 resident
+// 128-thread blocks per SM (80 registers; 5 warp-wide loads per round = 20
+// heads, e.g. 14 + 2 + 2), at 128 at least 5 (96 registers; 8 loads = 16
+// heads), both without spills. The kernel is issue-bound, so resident warps
+// matter more than loads in flight per warp.
+template <int D>
+constexpr int rope_min_blocks() {
+  return D == 64 ? 6 : 5;
+}
 
 // fp16 rows, head_dim 64 or 128: a warp per token, each lane owns 16 bytes
 // (8 dims) of a head, so one warp-wide load covers 32 / (D / 8) heads and the
@@ -376,12 +379,12 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(LayerArgs a, cons
 // lane group), RMS norms reduce over the group, and cos/sin are computed once
 // per token (lane k: pairs k and k + 32) and gathered by shuffles.
 template <int D>
-__global__ void __launch_bounds__(128, TLA_ROPE_MIN_BLOCKS) rope_rows_kernel(LayerArgs a, const __half* __restrict__ qkv,
+__global__ void __launch_bounds__(128, rope_min_blocks<D>()) rope_rows_kernel(LayerArgs a, const __half* __restrict__ qkv,
                                                         const int32_t* __restrict__ start, int seq_len, int tokens,
                                                         __half* __restrict__ qscr) {
   constexpr int L = D / 8;     // lanes per head
   constexpr int HPW = 32 / L;  // heads per warp-wide load
-  constexpr int kLoads = TLA_ROPE_LOADS;  // warp-wide loads in flight per round
+  constexpr int kLoads = D == 64 ? 5 : 8;  // warp-wide loads in flight per round
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int ti = blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -408,20 +411,29 @@ __global__ void __launch_bounds__(128, TLA_ROPE_MIN_BLOCKS) rope_rows_kernel(Lay
   float c0 = 1.f, s0 = 0.f, c1 = 1.f, s1 = 0.f;
   if (lane < a.pair_count && lane < half) rope_cos_sin(pos, a.inv_freq[lane], &c0, &s0);
   if (lane + 32 < a.pair_count && lane + 32 < half) rope_cos_sin(pos, a.inv_freq[lane + 32], &c1, &s1);
+  // cos/sin of this lane's 8 dims, with the attention factor folded in
   float cs[8], sn[8];
   bool turn[8];
   const int jb = lo_side ? d0 : d0 - half;
+  const bool wide = half > 32;  // pairs 32.. exist (the same for every thread)
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int j = jb + e, src = j & 31;
-    const float cc0 = __shfl_sync(full, c0, src), ss0 = __shfl_sync(full, s0, src);
-    const float cc1 = __shfl_sync(full, c1, src), ss1 = __shfl_sync(full, s1, src);
+    float cc = __shfl_sync(full, c0, src), ss = __shfl_sync(full, s0, src);
+    if (wide) {
+      const float cc1 = __shfl_sync(full, c1, src), ss1 = __shfl_sync(full, s1, src);
+      if (j >= 32) {
+        cc = cc1;
+        ss = ss1;
+      }
+    }
     turn[e] = rot && j < a.pair_count;
-    cs[e] = j < 32 ? cc0 : cc1;
-    sn[e] = j < 32 ? ss0 : ss1;
+    cs[e] = cc * a.attn_factor;
+    sn[e] = ss * a.attn_factor;
   }
   __half* kc = static_cast<__half*>(a.k_cache);
   __half* vc = static_cast<__half*>(a.v_cache);
+  const bool any_norm = a.q_norm != nullptr || a.k_norm != nullptr || a.v_norm != 0;
   for (int h0 = 0; h0 < heads; h0 += kLoads * HPW) {
     if (h0 > 0) {
 #pragma unroll
@@ -444,10 +456,12 @@ __global__ void __launch_bounds__(128, TLA_ROPE_MIN_BLOCKS) rope_rows_kernel(Lay
       const float* w = hh < Hq ? a.q_norm : (hh < Hq + Hk ? a.k_norm : nullptr);
       const bool norm = hh < Hq + Hk ? w != nullptr : a.v_norm != 0;
       float ss = 0.f;
+      if (any_norm) {  // the same for every thread: the shuffles stay warp-wide
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
+        for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
 #pragma unroll
-      for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(full, ss, o);
+        for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(full, ss, o);
+      }
       if (norm) {  // math.ts:78-97
         const float inv_rms = 1.f / sqrtf(ss / static_cast<float>(D) + a.rms_eps);
 #pragma unroll
@@ -462,7 +476,7 @@ __global__ void __launch_bounds__(128, TLA_ROPE_MIN_BLOCKS) rope_rows_kernel(Lay
       if (hh < Hq + Hk) {  // RoPE, math.ts:134-147
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          if (turn[e]) x[e] = (x[e] * cs[e] + (lo_side ? -pt[e] : pt[e]) * sn[e]) * a.attn_factor;
+          if (turn[e]) x[e] = x[e] * cs[e] + (lo_side ? -pt[e] : pt[e]) * sn[e];
       }
       if (hh >= heads) continue;
       uint4 outv;
