@@ -134,25 +134,6 @@ __device__ unsigned long long g_prefill_trace[64][16];
   } while (0)
 #endif
 
-#ifndef TLA_PREFILL_HELPER_NAP
-#define TLA_PREFILL_HELPER_NAP 0  // > 0: the TMA and MMA warps poll with this __nanosleep (ns) between tests
-#endif
-
-// Bounded poll with a sleep of `ns` between tests (for the helper warps, which
-// share sub-partitions with the softmax warps).
-__device__ __forceinline__ bool nap_wait(uint64_t* bar, uint32_t parity, int* err, int ns) {
-  if (mbar_test_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  for (int i = 0;; ++i) {
-    __nanosleep(ns);
-    if (mbar_test_wait(bar, parity)) return true;
-    if ((i & 63) == 63 && globaltimer() - t0 > kWaitLimitNs) {
-      report_error(err, TLA_ERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
 #ifndef TLA_PREFILL_POLY_EVERY
 #define TLA_PREFILL_POLY_EVERY 0  // every n-th pair of exponentials goes to the FMA pipe (0: none)
 #endif
@@ -340,14 +321,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     if (*abort_flag) return;
     if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
   };
-  auto hwait = [&](uint64_t* bar, uint32_t parity) {  // the TMA and MMA warps' waits
-#if TLA_PREFILL_HELPER_NAP > 0
-    if (*abort_flag) return;
-    if (!nap_wait(bar, parity, p.error, TLA_PREFILL_HELPER_NAP)) *abort_flag = 1;
-#else
-    wait(bar, parity);
-#endif
-  };
 
   if (warp == kTmaWarp) {
     // ================================================================ TMA producer
@@ -368,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         const int z = w.b * p.Hk + w.h / p.G;
         if (lane == 0) {
           const int qi = k % C::kNQ;
-          hwait(&q_empty[qi], ((k / C::kNQ) & 1) ^ 1);
+          wait(&q_empty[qi], ((k / C::kNQ) & 1) ^ 1);
           if (!*abort_flag) {
             mbar_arrive_expect_tx(&q_full[qi], C::kTile);
 #pragma unroll
@@ -379,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
         for (int n = 0; n < w.N; ++n, ++g) {
           const int st = g % C::kST;
-          hwait(&empty[st], ((g / C::kST) & 1) ^ 1);
+          wait(&empty[st], ((g / C::kST) & 1) ^ 1);
           if (!*abort_flag) {
             mbar_arrive_expect_tx(&full[st], C::kTile);
 #pragma unroll
@@ -389,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
       }
       for (int q = max(0, g - C::kST); q < g; ++q)  // no copies in flight at exit
-        hwait(&full[q % C::kST], (q / C::kST) & 1);
+        wait(&full[q % C::kST], (q / C::kST) & 1);
     }
   } else if (warp == kMmaWarp || warp == kSWarp) {
     // ================================================================ MMA issuers
@@ -403,11 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       constexpr uint32_t kIdS = idesc_f16(128, kT, false);
       constexpr uint32_t kIdO = idesc_f16(128, D, true);
       auto spin = [&](uint64_t* bar, uint32_t parity) {
-#if TLA_PREFILL_HELPER_NAP > 0
-        hwait(bar, parity);
-#else
         if (!*abort_flag && !mbar_spin(bar, parity, p.error)) *abort_flag = 1;
-#endif
       };
       // Descriptors are linear in the start address (bits 0-13 = addr >> 4, no
       // carry below 256 KB), so buffer, stage, box and k-step offsets are plain adds.
@@ -421,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         while (its >= 0) {  // S(gs) = Q K(gs)^T into buffer gs % NS
           // P V(gs - NS) has read P from this buffer (its barrier last
           // completed for P V(gs - NS - 2), which the previous wait covers)
-          if (gs >= NS) hwait(&o_done[(gs - NS) & 1], ((gs - NS) >> 1) & 1);
+          if (gs >= NS) wait(&o_done[(gs - NS) & 1], ((gs - NS) >> 1) & 1);
           if (ns == 0) spin(&q_full[ks % C::kNQ], (ks / C::kNQ) & 1);
           const int st = gs % C::kST;
           spin(&k_full[st], (gs / C::kST) & 1);
@@ -461,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           // the softmax step is usually still running: sleep on the barrier
           // instead of spinning, which would take issue slots from the softmax
           // warp on this sub-partition
-          hwait(&p_full[gp % NS], (gp / NS) & 1);
+          wait(&p_full[gp % NS], (gp / NS) & 1);
           tc_fence_after();
           PTRACE(10, gp);
           const uint64_t vb = dv + static_cast<uint64_t>(st * (C::kTile >> 4));
