@@ -53,6 +53,15 @@ def test_prefill_chunk_after_cached_prefix(pkg, cuda, D):
                  oracle_kw={"rope_theta": 1e6})
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_prefill_fp32_io_tensor_core_path(pkg, cuda, D):
+    # float32 qkv and outputs over the fp16 cache: the tensor-core kernel with
+    # 32-bit output rows (at head_dim 64 they leave through the shared-memory
+    # stage as 256-byte rows); 200 tokens leave partial last query tiles
+    prefill_case(pkg, cuda, 8, 2, D, 200, [0, 37], 512, dtype=torch.float32, layer_kw={"ropeTheta": 5e5},
+                 oracle_kw={"rope_theta": 5e5})
+
+
 def test_prefill_sliding_window_and_qk_norm(pkg, cuda):
     rng = np.random.default_rng(2)
     qn = rng.standard_normal(64).astype(np.float32) * 0.1

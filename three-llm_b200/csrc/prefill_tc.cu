@@ -147,6 +147,29 @@ __device__ __forceinline__ constexpr bool poly_pair(int i) {
 #endif
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two
+// columns' FMA or add, each element rounded as its scalar counterpart).
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+// (a0, a1) * b2 + c2
+__device__ __forceinline__ void fma_f32x2(float a0, float a1, uint64_t b2, uint64_t c2, float& r0, float& r1) {
+  asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%2, %3};\n\tfma.rn.f32x2 d, a, %4, %5;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "l"(b2), "l"(c2));
+}
+// acc += (e0, e1)
+__device__ __forceinline__ void add_f32x2(uint64_t& acc, float e0, float e1) {
+  asm("{\n\t.reg .b64 e;\n\tmov.b64 e, {%1, %2};\n\tadd.rn.f32x2 %0, %0, e;\n\t}" : "+l"(acc) : "f"(e0), "f"(e1));
+}
+__device__ __forceinline__ float sum_f32x2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+
 // 64 consecutive fp32 columns of this thread's TMEM lane (two loads, one wait).
 __device__ __forceinline__ void tmem_ld64x(uint32_t taddr, uint32_t (&r)[64]) {
 #pragma unroll
@@ -625,7 +648,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           m_run = m_new;
         }
         const float mu = m_run == -INFINITY ? 0.f : m_run;
-        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+        // x = S * scale_log2 - mu and the row sum, two columns per instruction
+        const uint64_t sl2x2 = pack_f32x2(sl2, sl2), nmu2 = pack_f32x2(-mu, -mu);
+        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t pk[32];
@@ -633,16 +658,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           for (int i = 0; i < 64; i += 2) {
             const int kc = 64 * c + i;
             const bool poly = poly_pair(kc / 2);
-            const float x0 = fmaf(__uint_as_float(sv[kc]), sl2, -mu);
-            const float x1 = fmaf(__uint_as_float(sv[kc + 1]), sl2, -mu);
+            float x0, x1;
+            fma_f32x2(__uint_as_float(sv[kc]), __uint_as_float(sv[kc + 1]), sl2x2, nmu2, x0, x1);
             const float e0 = poly ? ex2_poly(x0) : ex2(x0);
             const float e1 = poly ? ex2_poly(x1) : ex2(x1);
-            sum[(i >> 1) & 3] += e0 + e1;
+            add_f32x2(sum2[(i >> 1) & 3], e0, e1);
             pk[i / 2] = pack_half2(e0, e1);
           }
           tmem_st32(buf + 32 * c, pk);
         }
-        l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+        l_run += (sum_f32x2(sum2[0]) + sum_f32x2(sum2[1])) + (sum_f32x2(sum2[2]) + sum_f32x2(sum2[3]));
         if (lane == 0) PTRACE(3 + warp, g);
         pend_j = j;
         if (n == 0 && e_k >= 0) {  // the previous item's epilogue (its last P V is done by now)
