@@ -7,8 +7,9 @@
 // with every earlier prompt token already appended. This kernel computes the
 // same outputs for a whole prompt chunk at once: a RoPE/append kernel
 // (generic.cu) first writes the rotated queries (fp16, [B][Hq][S][D]) and
-// appends the chunk's K/V to the cache, then prefill_tc_kernel runs one CTA per
-// (128-row query tile, head, sequence), longest tiles first.
+// appends the chunk's K/V to the cache, then prefill_tc_kernel runs one
+// persistent CTA per SM over the work items (128-row query tile, head,
+// sequence), longest first.
 // Every mbarrier wait is bounded; on timeout the CTA records TLA_ERR_TIMEOUT,
 // stops waiting, runs its remaining control flow and frees its TMEM.
 #include <math.h>
@@ -209,9 +210,11 @@ __device__ __forceinline__ void tmem_ld64x(uint32_t taddr, uint32_t (&r)[64]) {
 // Softmax thread = one query row (TMEM lane), all 128 columns of the step in
 // registers (one pass). P(g) is written as fp16 pairs over the first 64
 // columns of its own S buffer and read from there as the A operand of P V;
-// S(g+NS) reuses the buffer only after P V(g) was issued. (Splitting the
-// columns over two warps per sub-partition, with a per-step exchange of the
-// row maxima, measured slower.) O accumulates in TMEM, double-buffered by
+// S(g+NS) reuses the buffer only after P V(g) has completed. The scale and
+// subtract and the row sums run as packed fp32 pairs. (Splitting the columns
+// over two warps per sub-partition, with a per-step exchange of the row
+// maxima, gained about 2% for eight more warps and was not kept.) O
+// accumulates in TMEM, double-buffered by
 // item where TMEM has room (head_dim 64), so the next item's P V can start
 // before this item's epilogue has read its O (o_free); likewise the Q tile in
 // shared memory (head_dim 64; at 128 the K/V stages take the room). A row's reference maximum only moves when a step's maximum
