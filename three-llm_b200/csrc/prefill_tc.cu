@@ -121,9 +121,9 @@ __device__ __forceinline__ float ex2_poly(float x) {
 // Optional pipeline trace (builds with -DTLA_PREFILL_TRACE only): SM clock of
 // each event of block 0's first 64 global steps, [step][event]; read with
 // tla_debug_prefill_trace. Softmax (warp 0 unless noted): [0] S(g) complete,
-// [1] P V(g-2) complete, [2] S(g) loaded, [3 + w] warp w's P(g) stored. MMA
-// issuer: [8]/[9] S(g) issue start/end, [12]/[13] before/after the V(g)
-// wait, [10]/[11] P V(g) issue start/end.
+// [1] after the fence that follows it, [2] S(g) loaded, [3 + w] warp w's P(g)
+// stored. S issuer: [8]/[9] S(g) issue start/end. P V issuer: [12]/[13]
+// before/after the V(g) wait, [10]/[11] P V(g) issue start/end.
 __device__ unsigned long long g_prefill_trace[64][16];
 #define PTRACE(ev, n) \
   do { \
