@@ -111,7 +111,10 @@ int tla_create(int device, tla_ctx** out);
 int tla_destroy(tla_ctx* ctx);
 
 /* Device-reported errors since the last reset (synchronises the device).
- * Replaces the reference's absence of a GPU error channel. */
+ * Replaces the reference's absence of a GPU error channel. With reset != 0
+ * the error word is cleared and, when an error was recorded, so are the
+ * context's split-KV completion counters, so the next launch on the context
+ * starts from a clean state. */
 int tla_get_error(tla_ctx* ctx, int reset);
 
 /* ropeParameters (packages/three-llm/src/runtime/rope.ts:4-52):
@@ -142,14 +145,35 @@ int tla_layer_cache_view(const tla_layer* layer, tla_cache_view* view);
 int tla_decode(tla_layer* layer, const void* qkv, const int32_t* positions, const void* gate, void* out,
                int32_t batch, void* stream);
 
+/* queryAttribute (TSLAttention.ts:53, written by the query kernel :288-304):
+ * the rotated queries of a decode step, QK-norm then RoPE at positions[b]
+ * exactly as tla_decode forms them, as float32 [batch][head_count][head_dim].
+ * Reads qkv only (nothing is appended). */
+int tla_query(tla_layer* layer, const void* qkv, const int32_t* positions, float* query_out, int32_t batch,
+              void* stream);
+
+/* scoreAttribute (TSLAttention.ts:52, written by the score kernel :306-356):
+ * scores_out[b][h][t] = attnScale * <query[b][h], K[b][kv(h)][t]> for every
+ * cache slot t in [window start, positions[b]], over the cache as it holds
+ * now (so after tla_decode it includes the appended token); slots outside
+ * that range are left untouched, as in the reference's buffer.
+ *   query      device float32 [batch][head_count][head_dim] (tla_query's output)
+ *   scores_out device float32 [batch][head_count][max_tokens]
+ * An inspection and test path: tla_decode never materialises its scores. */
+int tla_scores(tla_layer* layer, const float* query, const int32_t* positions, float* scores_out, int32_t batch,
+               void* stream);
+
 /* Causal prefill of seq_len tokens per sequence starting at start_pos[b]:
  * equal to seq_len decode steps at start_pos[b] + t
- * (DecoderTSLRunner.prefillTokens, packages/three-llm/src/decoder/DecoderTSLRunner.ts:504-530).
- *   qkv device [batch][seq_len][head_count + 2*kv_head_count][head_dim]
- *   out device [batch][seq_len][head_count][head_dim]
- *   start_pos device int32 [batch] */
-int tla_prefill(tla_layer* layer, const void* qkv, const int32_t* start_pos, int32_t seq_len, void* out,
-                int32_t batch, void* stream);
+ * (DecoderTSLRunner.prefillTokens, packages/three-llm/src/decoder/DecoderTSLRunner.ts:504-530,
+ * which replays the one-token graph, output gate included, per prompt position).
+ *   qkv       device [batch][seq_len][head_count + 2*kv_head_count][head_dim]
+ *   start_pos device int32 [batch]
+ *   gate      device [batch][seq_len][head_count][head_dim] or NULL
+ *             (gateNode, TSLAttention.ts:418-423: out *= sigmoid(gate))
+ *   out       device [batch][seq_len][head_count][head_dim] */
+int tla_prefill(tla_layer* layer, const void* qkv, const int32_t* start_pos, const void* gate, int32_t seq_len,
+                void* out, int32_t batch, void* stream);
 
 /* Sequence-sharded decode building block: attend over cache slots
  * [0, local_tokens) that hold global positions [slot_offset, slot_offset +

@@ -91,7 +91,7 @@ def lib():
         L.orc_rms_norm_packed_heads.restype = None
         L.orc_causal_attention.argtypes = [P, i32, P, P, P, P, P]
         L.orc_decode_batch.argtypes = [P, P, i32, i32, P, P, P, P, P, i32]
-        L.orc_prefill.argtypes = [P, P, i32, i32, i32, P, P, P, P, i32]
+        L.orc_prefill.argtypes = [P, P, P, i32, i32, i32, P, P, P, P, i32]
         L.orc_attend_heads.argtypes = [P, P, i32, i32, P, P, P, i32, i32, P, i32]
         _lib = L
     return _lib
@@ -221,15 +221,19 @@ def decode_batch(qkv, positions, key_cache, value_cache, gate=None, threads=1, *
     return out
 
 
-def prefill(qkv, start_pos, key_cache, value_cache, threads=1, **opts):
-    """Sequential-token prefill. qkv [B, S, (Hq+2Hk)*D]; caches [B, max_tokens, Hk*D] (in place)."""
+def prefill(qkv, start_pos, key_cache, value_cache, gate=None, threads=1, **opts):
+    """Prefill as the reference's token-by-token replay. qkv [B, S, (Hq+2Hk)*D];
+    gate None or [B, S, Hq*D]; caches [B, max_tokens, Hk*D] float32 (in place)."""
     o, keep = make_options(**opts)
     q = _f32(qkv)
     B, S = q.shape[0], q.shape[1]
     sp = np.ascontiguousarray(start_pos, dtype=np.int32)
+    g = None if gate is None else _f32(gate)
+    assert key_cache.dtype == np.float32 and key_cache.flags.c_contiguous
+    assert value_cache.dtype == np.float32 and value_cache.flags.c_contiguous
     out = np.zeros((B, S, o.head_count * o.head_dim), dtype=np.float32)
-    _check(lib().orc_prefill(_ptr(q), _ptr(sp), B, S, key_cache.shape[1], _ptr(key_cache), _ptr(value_cache),
-                             ctypes.byref(o), _ptr(out), int(threads)))
+    _check(lib().orc_prefill(_ptr(q), _ptr(sp), _ptr(g), B, S, key_cache.shape[1], _ptr(key_cache),
+                             _ptr(value_cache), ctypes.byref(o), _ptr(out), int(threads)))
     return out
 
 

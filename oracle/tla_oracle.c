@@ -284,22 +284,30 @@ int orc_decode_batch(const float* qkv, const int32_t* positions, int32_t batch, 
   return rc;
 }
 
-int orc_prefill(const float* qkv, const int32_t* start_pos, int32_t batch, int32_t seq_len, int32_t max_tokens,
-                float* key_cache, float* value_cache, const orc_attn_options* o, float* out, int32_t threads) {
+int orc_prefill(const float* qkv, const int32_t* start_pos, const float* gate, int32_t batch, int32_t seq_len,
+                int32_t max_tokens, float* key_cache, float* value_cache, const orc_attn_options* o, float* out,
+                int32_t threads) {
   if (!o || batch < 0 || seq_len < 0 || max_tokens <= 0) return ORC_ERR_ARG;
   const int32_t D = o->head_dim, Hq = o->head_count, Hk = o->kv_head_count;
   const size_t row = (size_t)(Hq + 2 * Hk) * D, q_size = (size_t)Hq * D;
   const size_t cache_seq = (size_t)max_tokens * Hk * D;
   for (int32_t b = 0; b < batch; b++)
     if (start_pos[b] < 0 || (int64_t)start_pos[b] + seq_len > max_tokens) return ORC_ERR_ARG;
+  const size_t tokens = (size_t)batch * seq_len;
+  float* q = (float*)malloc(sizeof(float) * q_size * (tokens > 0 ? tokens : 1));
   int rc = ORC_OK;
   set_threads(threads);
+  /* The reference replays causalAttention (math.ts:179-276) token by token.
+   * Token t's attention reads cache slots [window start, start + t] only, all
+   * written by then, so running every token's QK-norm / RoPE / append first
+   * (in token order within a sequence) and the attention of all
+   * (token, head) pairs afterwards gives the same values as the replay. */
 #pragma omp parallel for schedule(dynamic, 1) if (threads > 1)
   for (int32_t b = 0; b < batch; b++) {
     for (int32_t t = 0; t < seq_len; t++) {
-      int r = orc_causal_attention(qkv + ((size_t)b * seq_len + t) * row, start_pos[b] + t,
-                                   key_cache + b * cache_seq, value_cache + b * cache_seq, o, NULL,
-                                   out + ((size_t)b * seq_len + t) * q_size);
+      const size_t i = (size_t)b * seq_len + t;
+      int r = prepare_token(qkv + i * row, start_pos[b] + t, key_cache + b * cache_seq, value_cache + b * cache_seq,
+                            o, q + i * q_size);
       if (r != ORC_OK) {
 #pragma omp critical
         rc = r;
@@ -307,6 +315,17 @@ int orc_prefill(const float* qkv, const int32_t* start_pos, int32_t batch, int32
       }
     }
   }
+  if (rc == ORC_OK) {
+    const int64_t items = (int64_t)tokens * Hq;
+#pragma omp parallel for schedule(dynamic, 64) if (threads > 1)
+    for (int64_t it = 0; it < items; it++) {
+      const size_t i = (size_t)(it / Hq);
+      const int32_t h = (int32_t)(it % Hq), b = (int32_t)(i / (size_t)seq_len), t = (int32_t)(i % (size_t)seq_len);
+      attend_head(q + i * q_size, start_pos[b] + t, key_cache + b * cache_seq, value_cache + b * cache_seq, o, h,
+                  gate ? gate + i * q_size : NULL, out + i * q_size);
+    }
+  }
+  free(q);
   return rc;
 }
 

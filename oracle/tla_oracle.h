@@ -107,10 +107,14 @@ int orc_decode_batch(const float* qkv, const int32_t* positions, int32_t batch, 
                      float* key_cache, float* value_cache, const orc_attn_options* o,
                      const float* gate, float* out, int32_t threads);
 
-/* Prefill as the reference runs it: S one-token steps at start_pos[b]+t.
- * qkv [B][S][Hq+2Hk][D], out [B][S][Hq*D]. Sequences run in parallel
- * (threads > 1); positions within a sequence run in order. */
-int orc_prefill(const float* qkv, const int32_t* start_pos, int32_t batch, int32_t seq_len,
+/* Prefill as the reference runs it: S one-token steps at start_pos[b]+t
+ * (decoder/DecoderTSLRunner.ts:472-480, 504-530), each with the decode
+ * graph's output gate when gate != NULL.
+ * qkv [B][S][Hq+2Hk][D], gate NULL or [B][S][Hq*D], out [B][S][Hq*D].
+ * The per-token norm / RoPE / append steps run in token order within a
+ * sequence; the attention of the (token, head) pairs runs on `threads`
+ * OpenMP threads. The values equal the token-by-token replay. */
+int orc_prefill(const float* qkv, const int32_t* start_pos, const float* gate, int32_t batch, int32_t seq_len,
                 int32_t max_tokens, float* key_cache, float* value_cache, const orc_attn_options* o,
                 float* out, int32_t threads);
 

@@ -298,47 +298,148 @@ def test_sequence_shards_combine_equals_full_decode(pkg, cuda, D):
     assert_close(out, exp, what="LSE combine of sequence shards")
 
 
-def test_config2_full_size_vs_torch_fp32(pkg, cuda):
-    """BASELINE config 2 at full size for one layer (batch 64, 4096 cached + 1 new, 32/8 heads,
-    d64, theta 5e5) against a float32 PyTorch restatement over the same cache contents."""
-    import math
-
-    from three_llm_b200.attention import rope_parameters
-    from tests.test_prefill_gpu import torch_rope
-
-    torch.backends.cuda.matmul.allow_tf32 = False
-    B, T, Hq, Hk, D = 64, 4096, 32, 8, 64
-    g = torch.Generator(device=cuda)
-    g.manual_seed(4)
-    layer = pkg.CUDAAttention(None, Hq * D, Hq, T + 1, {"headDim": D, "kvHeadCount": Hk, "ropeTheta": 5e5,
-                                                        "maxBatch": B, "dtype": torch.float16})
-    view = layer.cache_view()
-    n = B * Hk * (T + 1) * D
-
-    class Arr:
-        def __init__(self, ptr):
-            self.__cuda_array_interface__ = {"shape": (B, Hk, T + 1, D), "typestr": "<f2", "data": (ptr, False),
-                                             "version": 3}
-
-    kc = torch.as_tensor(Arr(view.key), device=cuda)
-    vc = torch.as_tensor(Arr(view.value), device=cuda)
-    kc.normal_(generator=g)
-    vc.normal_(generator=g)
-    qkv = torch.randn(B, (Hq + 2 * Hk) * D, generator=g, device=cuda).half()
-    pos = torch.full((B,), T, dtype=torch.int32, device=cuda)
-    out = layer.decode(qkv, pos).float()
+# ---------------------------------------------------------------- recovery and shared launch limits
+def test_counters_recover_after_error_launch(pkg, cuda):
+    """A launch whose positions are partly invalid (TLA_ERR_POSITION: those
+    sequences are skipped) over many CTA-spanning sequences, then a correct
+    launch on the same context: the second launch's split-KV tickets start
+    from clean counters and its output matches the oracle."""
+    rng = np.random.default_rng(12)
+    Hq, Hk, D, T, B = 32, 8, 64, 2048, 24
+    lengths = [int(x) for x in rng.integers(300, T - 1, size=B)]
+    kc = f16(rng.standard_normal((B, T, Hk * D)))
+    vc = f16(rng.standard_normal((B, T, Hk * D)))
+    layer = pkg.CUDAAttention(None, Hq * D, Hq, T, {"headDim": D, "kvHeadCount": Hk, "ropeTheta": 5e5,
+                                                    "maxBatch": B, "dtype": torch.float16})
+    for b in range(B):
+        layer.write_cache(b, 0, kc[b], vc[b])
+    qkv = f16(rng.standard_normal((B, (Hq + 2 * Hk) * D)))
+    qkv_d = torch.from_numpy(qkv).to(cuda, torch.float16)
+    bad = list(lengths)
+    bad[3], bad[17] = T + 5, -1
+    layer.decode(qkv_d, torch.tensor(bad, dtype=torch.int32, device=cuda))
+    assert layer.context.error() == -12  # TLA_ERR_POSITION; the reset also clears the counters
+    for b in range(B):  # undo the first launch's appends of the valid sequences
+        layer.write_cache(b, 0, kc[b], vc[b])
+    out = layer.decode(qkv_d, torch.tensor(lengths, dtype=torch.int32, device=cuda)).float().cpu().numpy()
     assert layer.context.error() == 0
-    inv, _ = rope_parameters(D, 5e5)
-    inv = torch.from_numpy(inv).to(cuda)
-    x = qkv.float().view(B, Hq + 2 * Hk, 1, D)
-    p1 = torch.tensor([T], device=cuda)
-    q = torch_rope(x[:, :Hq], p1, inv, D)                      # [B, Hq, 1, D]
-    knew = torch_rope(x[:, Hq:Hq + Hk], p1, inv, D).half()     # stored fp16 in the cache
-    assert bool(torch.all((kc[:, :, T:T + 1].float() - knew.float()).abs() <= 2e-3)), "appended key"
-    k = kc.float().repeat_interleave(Hq // Hk, dim=1)          # [B, Hq, T+1, D] (slot T = new key)
-    v = vc.float().repeat_interleave(Hq // Hk, dim=1)
-    s = (q @ k.transpose(-1, -2)) / math.sqrt(D)
-    ref = (torch.softmax(s, dim=-1) @ v).reshape(B, Hq * D)
-    err = (out - ref).abs()
-    assert bool(torch.all(err <= 2e-3 + 1e-2 * ref.abs())), f"max abs err {err.max().item():.3e}"
-    del n
+    exp = oracle.decode_batch(qkv, lengths, kc, vc, threads=8, **oracle_opts(Hq, Hk, D, rope_theta=5e5))
+    assert_close(out, exp, what="decode after an error launch")
+
+
+def test_dynamic_smem_limit_is_never_lowered(pkg, cuda):
+    """Every layer of one kernel instance shares its dynamic shared-memory
+    limit: a layer created later with a smaller batch must not lower it below
+    what an earlier layer's full-batch launch needs."""
+    rng = np.random.default_rng(13)
+    Hq, Hk, D, T = 32, 8, 64, 512
+    big = pkg.CUDAAttention(None, Hq * D, Hq, T, {"headDim": D, "kvHeadCount": Hk, "ropeTheta": 5e5,
+                                                  "maxBatch": 256, "dtype": torch.float16})
+    small = pkg.CUDAAttention(None, Hq * D, Hq, T, {"headDim": D, "kvHeadCount": Hk, "ropeTheta": 5e5,
+                                                    "maxBatch": 1, "dtype": torch.float16})
+    B = 256
+    lengths = [int(x) for x in rng.integers(1, T - 1, size=B)]
+    kc = f16(rng.standard_normal((B, T, Hk * D)))
+    vc = f16(rng.standard_normal((B, T, Hk * D)))
+    for b in range(B):
+        big.write_cache(b, 0, kc[b], vc[b])
+    qkv = f16(rng.standard_normal((B, (Hq + 2 * Hk) * D)))
+    out = big.decode(torch.from_numpy(qkv).to(cuda, torch.float16),
+                     torch.tensor(lengths, dtype=torch.int32, device=cuda)).float().cpu().numpy()
+    assert big.context.error() == 0
+    exp = oracle.decode_batch(qkv, lengths, kc, vc, threads=8, **oracle_opts(Hq, Hk, D, rope_theta=5e5))
+    assert_close(out, exp, what="full-batch launch after a smaller layer")
+    small.close()
+    big.close()
+
+
+# ---------------------------------------------------------------- queryAttribute / scoreAttribute
+ROPE_FIXTURE = None
+
+
+def rope_fixture():
+    global ROPE_FIXTURE
+    if ROPE_FIXTURE is None:
+        import json
+        from pathlib import Path
+
+        ROPE_FIXTURE = json.loads((Path(__file__).resolve().parent / "golden" / "rope_cases.json").read_text())
+    return ROPE_FIXTURE["cases"]
+
+
+@pytest.mark.parametrize("case", range(5))
+def test_query_attribute_matches_pinned_rotated_q(pkg, cuda, case):
+    """reference.browser.test.ts:41-67: one head of dim 8, theta 1e4 and the
+    case's RoPE scaling; after each compute() the rotated query
+    (queryAttribute) and the cached key equal the pinned Transformers values,
+    at the reference's tolerance (expectClose, test/reference.ts:39-47)."""
+    c = rope_fixture()[case]
+    node = torch.zeros(24, dtype=torch.float32, device=cuda)
+    layer = pkg.CUDAAttention(node, 8, 1, 64, {"ropeTheta": c["theta"], "ropeScaling": c["scaling"],
+                                               "cacheDtype": "float32"})
+    for i, pos in enumerate(c["positions"]):
+        x = np.zeros(24, np.float32)
+        x[:8] = c["query"][i]
+        x[8:16] = c["key"][i]
+        node.copy_(torch.from_numpy(x))
+        layer.compute(None, pos)
+        assert_close(layer.queryAttribute, c["rotated_query"][i], 2e-5, 2e-4, f"{c['name']} query @ {pos}")
+        assert_close(layer.keyCacheAttribute[pos * 8:(pos + 1) * 8], c["rotated_key"][i], 2e-5, 2e-4,
+                     f"{c['name']} key @ {pos}")
+    assert layer.context.error() == 0
+
+
+def expected_scores(x, pos, kc, Hq, Hk, D, opts):
+    """attnScale * <Q'_h, K_t> over the window (test/gpu.ts cpuAttentionScores), from
+    the oracle's rotated query and its cache after the step."""
+    q = np.asarray(x[:Hq * D], np.float32).copy()
+    if opts.get("q_norm_weight") is not None:
+        for h in range(Hq):
+            q[h * D:(h + 1) * D] = oracle.rms_norm(q[h * D:(h + 1) * D], opts["q_norm_weight"],
+                                                   opts.get("rms_epsilon", 1e-6), opts.get("offset_rms_norm", False))
+    if opts.get("rope_theta"):
+        for h in range(Hq):
+            q = oracle.apply_rope(q, h * D, opts.get("rotary_dim", D), pos, opts["rope_theta"])
+    scale = opts.get("attn_scale", 1 / np.sqrt(D))
+    first = max(0, pos - opts["sliding_window"] + 1) if opts.get("sliding_window") else 0
+    s = {}
+    for h in range(Hq):
+        kvh = h * Hk // Hq
+        for t in range(first, pos + 1):
+            s[(h, t)] = scale * float(np.dot(q[h * D:(h + 1) * D].astype(np.float64),
+                                             kc[t, kvh * D:(kvh + 1) * D].astype(np.float64)))
+    return s
+
+
+@pytest.mark.parametrize("name,cache", [("mha", "float32"), ("gqa_rope", "float32"),
+                                        ("sliding_window_gqa", "float32"), ("qk_norm_rope", "float32"),
+                                        ("d64_gqa", "float16")])
+def test_score_attribute_matches_reference_scores(pkg, cuda, name, cache):
+    """test/gpu.ts:138-171 (assertAttentionSequence): after every step the score
+    buffer holds attnScale * <Q', K_t> for the window's tokens."""
+    if name == "mha":
+        Hq, Hk, D, T, kw, steps = 2, 2, 2, 4, {}, [[1, 0, 0, 1, 1, 0, 0, 1, 2, 3, 4, 5],
+                                                  [0, 1, 1, 0, 0, 1, 1, 0, 1, 1, 1, 1]]
+    elif name == "d64_gqa":
+        rng = np.random.default_rng(8)
+        Hq, Hk, D, T, kw = 8, 2, 64, 40, {"rope_theta": 10000.0}
+        steps = list(f16(rng.standard_normal((6, (Hq + 2 * Hk) * D))))
+    else:
+        Hq, Hk, D, T, seeds, kw = CAUSAL_CASES[name]
+        steps = [fill_sin((Hq + 2 * Hk) * D, s) for s in seeds]
+    layer, kc, vc = None, None, None
+    node = torch.zeros((Hq + 2 * Hk) * D, dtype=torch.float32, device=cuda)
+    layer = pkg.CUDAAttention(node, Hq * D, Hq, T, layer_options(Hk, D, cacheDtype=cache, **to_layer_options(kw)))
+    kc = np.zeros((T, Hk * D), np.float32)
+    vc = np.zeros_like(kc)
+    tol = (1e-4, 0) if cache == "float32" else (ATOL, RTOL)
+    for pos, x in enumerate(steps):
+        x = np.asarray(x, np.float32)
+        node.copy_(torch.from_numpy(x))
+        layer.compute(None, pos)
+        oracle.causal_attention(x, pos, kc, vc, **oracle_opts(Hq, Hk, D, **kw))
+        got = layer.scoreAttribute.reshape(Hq, T)
+        exp = expected_scores(x, pos, kc, Hq, Hk, D, kw)
+        keys = sorted(exp)
+        assert_close([got[h, t] for h, t in keys], [exp[k] for k in keys], tol[0], tol[1], f"{name} scores @ {pos}")
+    assert layer.context.error() == 0

@@ -2,7 +2,7 @@
 which replays the one-token step at positions start..start+S-1
 (packages/three-llm/src/decoder/DecoderTSLRunner.ts:504-530). Outputs for
 every position and the cache contents must agree with the oracle."""
-import math
+import os
 
 import numpy as np
 import pytest
@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 
 def prefill_case(pkg, cuda, Hq, Hk, D, S, starts, max_tokens, dtype=torch.float16, layer_kw=None, oracle_kw=None,
-                 seed=0, cache_dtype="float16"):
+                 seed=0, cache_dtype="float16", gate=False):
     rng = np.random.default_rng(seed)
     B = len(starts)
     row = (Hq + 2 * Hk) * D
@@ -23,15 +23,17 @@ def prefill_case(pkg, cuda, Hq, Hk, D, S, starts, max_tokens, dtype=torch.float1
     kc, vc = pre.copy(), f16(rng.standard_normal((B, max_tokens, Hk * D)))
     vpre = vc.copy()
     qkv = f16(rng.standard_normal((B, S, row)))
+    g = f16(rng.standard_normal((B, S, Hq * D)) * 2) if gate else None
     opts = {"headDim": D, "kvHeadCount": Hk, "maxBatch": B, "dtype": dtype, "cacheDtype": cache_dtype}
     opts.update(layer_kw or {})
     layer = pkg.CUDAAttention(None, Hq * D, Hq, max_tokens, opts)
     for b in range(B):
         layer.write_cache(b, 0, pre[b], vpre[b])
     sp = torch.tensor(starts, dtype=torch.int32, device=cuda)
-    out = layer.prefill(torch.from_numpy(qkv).to(cuda, dtype), sp).float().cpu().numpy()
-    exp = oracle.prefill(qkv, starts, kc, vc, threads=8, head_count=Hq, kv_head_count=Hk, head_dim=D,
-                         **(oracle_kw or {}))
+    out = layer.prefill(torch.from_numpy(qkv).to(cuda, dtype), sp,
+                        gate=None if g is None else torch.from_numpy(g).to(cuda, dtype)).float().cpu().numpy()
+    exp = oracle.prefill(qkv, starts, kc, vc, gate=g, threads=os.cpu_count(), head_count=Hq, kv_head_count=Hk,
+                         head_dim=D, **(oracle_kw or {}))
     assert layer.context.error() == 0
     assert_close(out, exp, what="prefill outputs")
     for b in range(B):
@@ -39,6 +41,23 @@ def prefill_case(pkg, cuda, Hq, Hk, D, S, starts, max_tokens, dtype=torch.float1
         assert_close(k, kc[b, starts[b]:starts[b] + S], 2e-3, 2e-3, "prefill key cache")
         assert_close(v, vc[b, starts[b]:starts[b] + S], 2e-3, 2e-3, "prefill value cache")
     return layer
+
+
+@pytest.mark.parametrize("D,dtype", [(64, torch.float16), (128, torch.float16), (64, torch.float32)])
+def test_prefill_output_gate(pkg, cuda, D, dtype):
+    # Qwen3.5 full-attention layers gate every prompt position's output
+    # (qwen/QwenTSLRunner.ts:172-186; the replayed decode graph applies
+    # gateNode, TSLAttention.ts:418-423): the fused sigmoid epilogue of the
+    # tensor-core kernel, 200 tokens leave a partial last query tile
+    qn = np.random.default_rng(4).standard_normal(D).astype(np.float32) * 0.1
+    prefill_case(pkg, cuda, 16, 4, D, 200, [0, 45], 512, dtype=dtype, gate=True,
+                 layer_kw={"ropeTheta": 1e6, "qNormWeight": qn, "kNormWeight": qn, "offsetRMSNorm": True},
+                 oracle_kw={"rope_theta": 1e6, "q_norm_weight": qn, "k_norm_weight": qn, "offset_rms_norm": True})
+
+
+def test_prefill_output_gate_generic_path(pkg, cuda):
+    prefill_case(pkg, cuda, 4, 2, 8, 19, [0, 3], 32, dtype=torch.float32, gate=True,
+                 layer_kw={"ropeTheta": 10000.0}, oracle_kw={"rope_theta": 10000.0}, cache_dtype="float32")
 
 
 def test_prefill_small_generic_shapes(pkg, cuda):
@@ -99,38 +118,23 @@ def test_prefill_partial_rotary_yarn_vnorm(pkg, cuda, rotary):
                  oracle_kw={"rope_theta": 10000.0, "rotary_dim": rotary, "rope_scaling": yarn, "v_norm": True})
 
 
-def torch_rope(x, pos, inv_freq, rotary, attn_factor=1.0):
-    """float32 rotate-half RoPE with float64 angles (x [..., T, D], pos [T])."""
-    ang = pos.double()[:, None] * inv_freq.double()[None, :]
-    c, s = torch.cos(ang).float(), torch.sin(ang).float()
-    half = rotary // 2
-    x1, x2, rest = x[..., :half], x[..., half:rotary], x[..., rotary:]
-    return torch.cat([(x1 * c - x2 * s) * attn_factor, (x2 * c + x1 * s) * attn_factor, rest], dim=-1)
-
-
-def test_prefill_config3_full_size_vs_torch_fp32(pkg, cuda):
-    """BASELINE config 3 at full size (4 x 2048 tokens, 14/2 heads, d64, theta 1e6)
-    against a float32 PyTorch restatement of the same causal attention."""
-    from three_llm_b200.attention import rope_parameters
-
-    torch.backends.cuda.matmul.allow_tf32 = False
+def test_prefill_config3_full_size_vs_oracle(pkg, cuda):
+    """BASELINE config 3 at full size (4 x 2048 tokens, 14/2 heads, d64, theta 1e6,
+    K/V into a 4096-slot cache) against the oracle's token-by-token replay."""
     B, S, Hq, Hk, D, T = 4, 2048, 14, 2, 64, 4096
-    g = torch.Generator(device=cuda)
-    g.manual_seed(3)
-    qkv = torch.randn(B, S, (Hq + 2 * Hk) * D, generator=g, device=cuda).half()
+    rng = np.random.default_rng(3)
+    qkv = f16(rng.standard_normal((B, S, (Hq + 2 * Hk) * D)))
     layer = pkg.CUDAAttention(None, Hq * D, Hq, T, {"headDim": D, "kvHeadCount": Hk, "ropeTheta": 1e6, "maxBatch": B,
                                                     "dtype": torch.float16})
-    out = layer.prefill(qkv, torch.zeros(B, dtype=torch.int32, device=cuda)).float()
+    out = layer.prefill(torch.from_numpy(qkv).to(cuda, torch.float16),
+                        torch.zeros(B, dtype=torch.int32, device=cuda)).float().cpu().numpy()
     assert layer.context.error() == 0
-    inv, _ = rope_parameters(D, 1e6)
-    inv = torch.from_numpy(inv).to(cuda)
-    x = qkv.float().view(B, S, Hq + 2 * Hk, D).transpose(1, 2)  # [B, H, S, D]
-    pos = torch.arange(S, device=cuda)
-    q = torch_rope(x[:, :Hq], pos, inv, D)
-    k = torch_rope(x[:, Hq:Hq + Hk], pos, inv, D).repeat_interleave(Hq // Hk, dim=1)
-    v = x[:, Hq + Hk:].repeat_interleave(Hq // Hk, dim=1)
-    s = (q @ k.transpose(-1, -2)) / math.sqrt(D)
-    s = s.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool, device=cuda), 1), float("-inf"))
-    ref = (torch.softmax(s, dim=-1) @ v).transpose(1, 2).reshape(B, S, Hq * D)
-    err = (out - ref).abs()
-    assert bool(torch.all(err <= 2e-3 + 1e-2 * ref.abs())), f"max abs err {err.max().item():.3e}"
+    kc = np.zeros((B, T, Hk * D), np.float32)
+    vc = np.zeros_like(kc)
+    exp = oracle.prefill(qkv, [0] * B, kc, vc, threads=os.cpu_count(), head_count=Hq, kv_head_count=Hk, head_dim=D,
+                         rope_theta=1e6)
+    assert_close(out, exp, what="config 3 prefill")
+    for b in (0, B - 1):
+        k, v = layer.read_cache(b, 0, S)
+        assert_close(k, kc[b, :S], 2e-3, 2e-3, "config 3 key cache")
+        assert_close(v, vc[b, :S], 2e-3, 2e-3, "config 3 value cache")

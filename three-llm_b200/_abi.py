@@ -1,8 +1,8 @@
 """ctypes binding of libtla.so (include/tla_api.h).
 
-This is the same binding a three-llm host would write over the C ABI (the
-N-API addon shown in INTEGRATION.md does the same in C++). There is no CPU
-fallback: loading fails loudly if the CUDA library has not been built.
+This is the same binding a three-llm host would write over the C ABI (an
+N-API addon in a Node host does the same in C++). There is no CPU fallback:
+loading fails loudly if the CUDA library has not been built.
 """
 import ctypes
 import os
@@ -32,6 +32,7 @@ EXPORTS = [
     "tla_decode_partial", "tla_combine_lse", "tla_cache_reset", "tla_cache_read", "tla_cache_write",
     "tla_decode_noalloc", "tla_exchange_create", "tla_exchange_connect", "tla_exchange_combine",
     "tla_exchange_buffer", "tla_exchange_connect_buffers", "tla_exchange_destroy", "tla_decode_exchange",
+    "tla_query", "tla_scores",
 ]
 
 
@@ -110,7 +111,9 @@ def lib():
         L.tla_layer_destroy.argtypes = [P]
         L.tla_layer_cache_view.argtypes = [P, ctypes.POINTER(CacheView)]
         L.tla_decode.argtypes = [P, P, P, P, P, i32, P]
-        L.tla_prefill.argtypes = [P, P, P, i32, P, i32, P]
+        L.tla_prefill.argtypes = [P, P, P, P, i32, P, i32, P]
+        L.tla_query.argtypes = [P, P, P, P, i32, P]
+        L.tla_scores.argtypes = [P, P, P, P, i32, P]
         L.tla_decode_partial.argtypes = [P, P, P, i32, i32, i32, P, i32, P]
         L.tla_combine_lse.argtypes = [P, i32, i32, i32, i32, P, P, u32, P]
         L.tla_cache_reset.argtypes = [P, P]

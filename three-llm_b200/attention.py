@@ -148,6 +148,8 @@ class CUDAAttention:
         self.outputNode = torch.empty(self.qSize, dtype=dtype, device=self.device)
         self.outputAttribute = self.outputNode
         self._position = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._last_position = None   # the position tensor of the last compute()
+        self._score_buf = None       # scoreAttribute's buffer, created on first read
         self.computeNodes = [self]   # one fused launch (orderedComputeNodes keeps working)
         self.computeNode = self
 
@@ -165,7 +167,34 @@ class CUDAAttention:
         pos = self.positionNode if self.positionNode is not None else self._position
         self.decode(self.qkvNode.view(1, -1), pos, gate=None if self.gateNode is None else self.gateNode.view(1, -1),
                     out=self.outputNode.view(1, -1), stream=stream)
+        self._last_position = pos
         return self.outputNode
+
+    def _step_inputs(self):
+        if self._last_position is None:
+            raise RuntimeError("compute() has not run yet")
+        return self.qkvNode.view(1, -1), self._last_position.view(1)
+
+    @property
+    def queryAttribute(self):
+        """queryAttribute (TSLAttention.ts:53): the last compute() step's rotated
+        queries, float32 [Hq * headDim], formed by tla_query from the qkv node and
+        position that step used (QK-norm, then RoPE, as the decode forms them)."""
+        qkv, pos = self._step_inputs()
+        return self.query(qkv, pos)[0].cpu().numpy()
+
+    @property
+    def scoreAttribute(self):
+        """scoreAttribute (TSLAttention.ts:52): float32 [Hq * maxTokens] with the
+        last compute() step's scaled scores at the slots of its window
+        [start, position] of sequence 0 (tla_scores over the cache, new token
+        included); other slots keep what earlier reads left (zero at first), as
+        the reference's score buffer does."""
+        qkv, pos = self._step_inputs()
+        if self._score_buf is None:
+            self._score_buf = torch.zeros(1, self.headCount, self.maxTokens, dtype=torch.float32, device=self.device)
+        self.scores(self.query(qkv, pos), pos, out=self._score_buf)
+        return self._score_buf.view(-1).cpu().numpy()
 
     def reset(self, stream=None):
         """reset() (TSLAttention.ts:434-441)."""
@@ -227,15 +256,36 @@ class CUDAAttention:
               "decode")
         return out
 
-    def prefill(self, qkv, start_pos, out=None, stream=None):
-        """Causal prefill: qkv [B, S, (Hq+2Hk)*D], start_pos int32 [B]; out [B, S, Hq*D]."""
+    def query(self, qkv, positions, out=None, stream=None):
+        """Rotated queries of a decode step (tla_query): float32 [B, Hq*D], nothing appended."""
+        B = qkv.shape[0]
+        self._check_io(qkv, "qkv")
+        if out is None:
+            out = torch.empty(B, self.qSize, dtype=torch.float32, device=self.device)
+        check(lib().tla_query(self.handle, _ptr(qkv), _ptr(positions), _ptr(out), B, _stream(stream)), "query")
+        return out
+
+    def scores(self, query, positions, out=None, stream=None):
+        """Scaled scores over each sequence's window (tla_scores): float32 [B, Hq, maxTokens];
+        slots outside [window start, position] keep out's previous contents (zeros if out is None)."""
+        B = query.shape[0]
+        if out is None:
+            out = torch.zeros(B, self.headCount, self.maxTokens, dtype=torch.float32, device=self.device)
+        check(lib().tla_scores(self.handle, _ptr(query.contiguous()), _ptr(positions), _ptr(out), B,
+                               _stream(stream)), "scores")
+        return out
+
+    def prefill(self, qkv, start_pos, gate=None, out=None, stream=None):
+        """Causal prefill: qkv [B, S, (Hq+2Hk)*D], start_pos int32 [B], gate None or
+        [B, S, Hq*D] (out *= sigmoid(gate) at every position); out [B, S, Hq*D]."""
         B, S = qkv.shape[0], qkv.shape[1]
         self._check_io(qkv, "qkv")
+        self._check_io(gate, "gate")
         if out is None:
             out = torch.empty(B, S, self.qSize, dtype=self.dtype, device=self.device)
         self._check_io(out, "out")
-        check(lib().tla_prefill(self.handle, _ptr(qkv), _ptr(start_pos), S, _ptr(out), B, _stream(stream)),
-              "prefill")
+        check(lib().tla_prefill(self.handle, _ptr(qkv), _ptr(start_pos), _ptr(gate), S, _ptr(out), B,
+                                _stream(stream)), "prefill")
         return out
 
     def decode_partial(self, qkv, positions, slot_offset, local_tokens, append, partial=None, stream=None):

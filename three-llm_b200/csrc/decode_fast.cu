@@ -1212,12 +1212,14 @@ cudaError_t launch_t(const tla_layer* L, const DecodeParams& p, const ExchangeDe
 
 template <int D, typename IO, bool TWO>
 cudaError_t configure_t(tla_layer* L, int* blocks) {
+  // A launch of `batch` sequences uses smem_layout(G, batch) <= this layer's
+  // worst case; the limit is shared with every other layer on this instance.
   const SmemLayout s = smem_layout<D>(L->G, L->max_batch);
-  auto k = decode_fast_kernel<D, IO, TWO>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, s.total);
+  const void* k = reinterpret_cast<const void*>(decode_fast_kernel<D, IO, TWO>);
+  cudaError_t e = raise_smem_limit(k, s.total);
   if (e != cudaSuccess) return e;
   L->decode_smem = s.total;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k, kThreads, s.total);
+  return cached_occupancy(k, kThreads, s.total, blocks);
 }
 
 template <int D>
@@ -1347,6 +1349,13 @@ StaticScratchSlot g_static_slots[kStaticMaxDevices];
 std::once_flag g_static_encode_once;
 PFN_cuTensorMapEncodeTiled_v12000 g_static_encode = nullptr;
 
+// The RoPE table travels by value in the kernel parameters, so no host
+// buffer has to outlive the call.
+struct InvFreqTable {
+  float v[64];
+};
+__global__ void store_inv_freq_kernel(float* dst, InvFreqTable t) { dst[threadIdx.x] = t.v[threadIdx.x]; }
+
 }  // namespace
 }  // namespace tla
 
@@ -1371,11 +1380,11 @@ extern "C" int tla_decode_noalloc(const tla_attn_config* cfg, void* key_cache, v
   const bool rope_on = cfg->rope_theta > 0 && rotary > 0;
   const int freq_dim = cfg->rope_freq_dim > 0 ? cfg->rope_freq_dim : rotary;
   const int pair_count = cfg->rope_pair_count >= 0 ? cfg->rope_pair_count : rotary / 2;
-  float inv[64] = {0.f};
+  InvFreqTable inv = {};
   double af = 1;
   if (rope_on) {
     if (freq_dim / 2 > 64) return TLA_ERR_UNSUPPORTED;
-    const int rc = tla_rope_parameters(freq_dim, cfg->rope_theta, &cfg->rope_scaling, inv, &af);
+    const int rc = tla_rope_parameters(freq_dim, cfg->rope_theta, &cfg->rope_scaling, inv.v, &af);
     if (rc != TLA_OK) return rc;
     if (pair_count > freq_dim / 2) return TLA_ERR_INVALID_ARG;
   }
@@ -1442,7 +1451,8 @@ extern "C" int tla_decode_noalloc(const tla_attn_config* cfg, void* key_cache, v
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The array keeps the previous call's contents: reload the RoPE table and
   // zero the completion counters this launch uses.
-  if (cudaMemcpyAsync(L.d_inv_freq, inv, sizeof(inv), cudaMemcpyHostToDevice, st) != cudaSuccess) return TLA_ERR_CUDA;
+  store_inv_freq_kernel<<<1, 64, 0, st>>>(L.d_inv_freq, inv);
+  if (cudaGetLastError() != cudaSuccess) return TLA_ERR_CUDA;
   if (cudaMemsetAsync(ctx.d_counters, 0, sizeof(int32_t) * batch * Hk, st) != cudaSuccess) return TLA_ERR_CUDA;
   const cudaError_t e =
       launch_decode_fast(&L, qkv, positions, gate, out, nullptr, batch, 0, cfg->max_tokens, 1, st);

@@ -217,7 +217,7 @@ cudaError_t rope_append_t(const tla_layer* L, const void* qkv, const int32_t* st
   const size_t smem = sizeof(float) * (static_cast<size_t>(L->Hq + 2 * L->Hk) * L->D + 2 * (L->rotary / 2 + 1) + 4);
   auto k = rope_append_kernel<IO, CT, QH>;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(k), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
   k<<<dim3(seq_len, batch), kThreads, smem, stream>>>(a, static_cast<const IO*>(qkv), start, seq_len, slot_offset,
@@ -555,6 +555,48 @@ cudaError_t launch_attend_generic(const tla_layer* L, const float* qscr, const i
                                        stream)
              : attend_t<__half, __half>(L, qscr, start, batch, seq_len, slot_offset, local_tokens, gate, out, partial,
                                         stream);
+}
+
+// ---------------------------------------------------------------- scores (scoreAttribute)
+namespace {
+// One block per (h, b): the block's threads walk the window's slots; the
+// query row is staged in shared memory (TSLAttention.ts:306-356).
+template <typename CT>
+__global__ void __launch_bounds__(kThreads) scores_kernel(LayerArgs a, const float* __restrict__ query,
+                                                          const int32_t* __restrict__ positions,
+                                                          float* __restrict__ scores) {
+  extern __shared__ float q[];  // [D]
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int D = a.D, Hq = a.Hq, Hk = a.Hk;
+  const int pos = positions[b];
+  if (pos < 0 || pos >= a.max_tokens) {
+    if (threadIdx.x == 0) report_error(a.error, TLA_ERR_POSITION);
+    return;
+  }
+  const size_t qrow = static_cast<size_t>(b) * Hq + h;
+  for (int d = threadIdx.x; d < D; d += kThreads) q[d] = query[qrow * D + d];
+  __syncthreads();
+  const int kvh = static_cast<int>((static_cast<long long>(h) * Hk) / Hq);  // TSLAttention.ts:340
+  const int first = a.sliding > 0 ? max(0, pos - a.sliding + 1) : 0;       // :330-334
+  const CT* kc = static_cast<const CT*>(a.k_cache) + (static_cast<size_t>(b) * Hk + kvh) * a.max_tokens * D;
+  for (int t = first + threadIdx.x; t <= pos; t += kThreads) {
+    const CT* kr = kc + static_cast<size_t>(t) * D;
+    float dot = 0.f;
+    for (int d = 0; d < D; ++d) dot += q[d] * to_f32(kr[d]);
+    scores[qrow * a.max_tokens + t] = dot * a.attn_scale;
+  }
+}
+}  // namespace
+
+cudaError_t launch_scores(const tla_layer* L, const float* query, const int32_t* positions, int batch, float* scores,
+                          cudaStream_t stream) {
+  const LayerArgs a = layer_args(L);
+  const size_t smem = sizeof(float) * L->D;
+  if (L->cache_fp32)
+    scores_kernel<float><<<dim3(L->Hq, batch), kThreads, smem, stream>>>(a, query, positions, scores);
+  else
+    scores_kernel<__half><<<dim3(L->Hq, batch), kThreads, smem, stream>>>(a, query, positions, scores);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------- LSE combine

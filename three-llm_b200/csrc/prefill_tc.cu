@@ -29,6 +29,7 @@ struct PrefillParams {
   CUtensorMap tm_k;  // cache [max_batch*Hk][max_tokens][D] fp16, 128-token boxes
   CUtensorMap tm_v;
   void* out;
+  const void* gate;  // null, or [B][S][Hq][D] like out: out *= sigmoid(gate)
   const int32_t* start;
   int* error;
   int S, Hq, Hk, G, sliding, batch, num_m;
@@ -188,6 +189,32 @@ __device__ __forceinline__ void tmem_ld64x(uint32_t taddr, uint32_t (&r)[64]) {
           "=r"(r[k * 32 + 30]), "=r"(r[k * 32 + 31])
         : "r"(taddr + k * 32));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 consecutive values of a gate row, as floats (16-byte loads).
+template <typename T>
+__device__ __forceinline__ void load_row32(const T* src, float (&v)[32]) {
+  if constexpr (sizeof(T) == 2) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = *reinterpret_cast<const uint4*>(src + 8 * i);
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[8 * i + 2 * k] = __low2float(h[k]);
+        v[8 * i + 2 * k + 1] = __high2float(h[k]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 f = *reinterpret_cast<const float4*>(src + 4 * i);
+      v[4 * i] = f.x;
+      v[4 * i + 1] = f.y;
+      v[4 * i + 2] = f.z;
+      v[4 * i + 3] = f.w;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -517,6 +544,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const float inv = le > 0.f ? 1.f / le : 0.f;
       const size_t row_stride = static_cast<size_t>(p.Hq) * D;  // elements between consecutive tokens
       OUT* const dst0 = static_cast<OUT*>(p.out) + base;        // row 0 of the item's tile
+      // Output gate (TSLAttention.ts:418-423, math.ts:271-273): this row's 32
+      // columns times sigmoid(gate), in fp32 before the conversion to OUT.
+      auto gate_cols = [&](float (&o)[32], int c) {
+        if (p.gate == nullptr || r >= rows) return;
+        float gv[32];
+        load_row32(static_cast<const OUT*>(p.gate) + base + r * row_stride + 32 * c, gv);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = o[i] * (1.f / (1.f + expf(-gv[i])));
+      };
       if constexpr (C::kOutBytes > 0) {
         // Rows go through this warp's shared-memory stage (16-byte chunks
         // XOR-swizzled by row, so neither side has bank conflicts) and leave
@@ -530,6 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         for (int c = 0; c < D / 32; ++c) {
           float o[32];
           tmem_ld32(oe + 32 * c, o);
+          gate_cols(o, c);
 #pragma unroll
           for (int i = 0; i < kPer32; ++i) {
             uint4 v;
@@ -564,6 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         for (int c = 0; c < D / 32; ++c) {
           float o[32];
           tmem_ld32(oe + 32 * c, o);
+          gate_cols(o, c);
           if (r < rows) {
             OUT* dst = dst0 + r * row_stride + 32 * c;
             if constexpr (sizeof(OUT) == 2) {
@@ -708,7 +746,7 @@ CUresult make_map(const tla_layer* L, void* base, uint64_t rows, uint64_t planes
 
 template <int D, typename OUT>
 cudaError_t set_smem() {
-  return cudaFuncSetAttribute(prefill_tc_kernel<D, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<D>::kSmem);
+  return raise_smem_limit(reinterpret_cast<const void*>(prefill_tc_kernel<D, OUT>), PCfg<D>::kSmem);
 }
 
 }  // namespace
@@ -739,8 +777,8 @@ cudaError_t prefill_fast_configure(tla_layer* L) {
   return cudaSuccess;
 }
 
-cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
-                                void* out, cudaStream_t stream) {
+cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32_t* start, const void* gate, int batch,
+                                int seq_len, void* out, cudaStream_t stream) {
   __half* qh = static_cast<__half*>(L->ctx->d_qscratch);
   cudaError_t e = launch_rope_append_half_q(L, qkv, start, batch, seq_len, qh, stream);
   if (e != cudaSuccess) return e;
@@ -750,6 +788,7 @@ cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32
   p.tm_k = L->tmap_k128;
   p.tm_v = L->tmap_v128;
   p.out = out;
+  p.gate = gate;
   p.start = start;
   p.error = L->ctx->d_error;
   p.S = seq_len;

@@ -6,6 +6,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
 #include <vector>
 
 #include "tla_device.cuh"
@@ -38,6 +39,54 @@ LayerArgs layer_args(const tla_layer* L) {
   a.v_norm = L->v_norm ? 1 : 0;
   a.offset_rms = L->offset_rms ? 1 : 0;
   return a;
+}
+
+namespace {
+struct SmemLimit {
+  int device;
+  const void* kernel;
+  int bytes;
+};
+struct Occupancy {
+  int device;
+  const void* kernel;
+  int threads, smem, blocks;
+};
+std::mutex g_attr_mu;
+std::vector<SmemLimit> g_smem_limits;
+std::vector<Occupancy> g_occupancy;
+}  // namespace
+
+cudaError_t raise_smem_limit(const void* kernel, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(g_attr_mu);
+  for (SmemLimit& s : g_smem_limits) {
+    if (s.device != dev || s.kernel != kernel) continue;
+    if (bytes <= s.bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) s.bytes = bytes;
+    return e;
+  }
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) g_smem_limits.push_back({dev, kernel, bytes});
+  return e;
+}
+
+cudaError_t cached_occupancy(const void* kernel, int threads, int smem, int* blocks) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(g_attr_mu);
+  for (const Occupancy& o : g_occupancy)
+    if (o.device == dev && o.kernel == kernel && o.threads == threads && o.smem == smem) {
+      *blocks = o.blocks;
+      return cudaSuccess;
+    }
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kernel, threads, smem);
+  if (e == cudaSuccess) g_occupancy.push_back({dev, kernel, threads, smem, *blocks});
+  return e;
 }
 }  // namespace tla
 
@@ -205,7 +254,15 @@ int tla_get_error(tla_ctx* ctx, int reset) {
   int v = 0;
   e = cudaMemcpy(&v, ctx->d_error, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return from_cuda(e);
-  if (reset) cudaMemset(ctx->d_error, 0, sizeof(int));
+  if (reset) {
+    e = cudaMemset(ctx->d_error, 0, sizeof(int));
+    // A launch that reported an error may have ended before the CTA that
+    // completes a split (sequence, kv head) pair zeroed that pair's counter;
+    // the next launch's tickets need every counter at zero.
+    if (e == cudaSuccess && v != 0 && ctx->d_counters)
+      e = cudaMemset(ctx->d_counters, 0, ctx->counter_count * sizeof(int32_t));
+    if (e != cudaSuccess) return from_cuda(e);
+  }
   return v;
 }
 
@@ -358,8 +415,27 @@ int tla_decode(tla_layer* L, const void* qkv, const int32_t* positions, const vo
   return from_cuda(tla::launch_attend_generic(L, qs, positions, batch, 1, 0, L->max_tokens, gate, out, nullptr, st));
 }
 
-int tla_prefill(tla_layer* L, const void* qkv, const int32_t* start_pos, int32_t seq_len, void* out, int32_t batch,
-                void* stream) {
+int tla_query(tla_layer* L, const void* qkv, const int32_t* positions, float* query_out, int32_t batch,
+              void* stream) {
+  if (!valid_layer(L) || !qkv || !positions || !query_out || batch < 0 || batch > L->max_batch)
+    return TLA_ERR_INVALID_ARG;
+  if (batch == 0) return TLA_OK;
+  DeviceGuard g(L->ctx->device);
+  return from_cuda(tla::launch_rope_append(L, qkv, positions, batch, 1, 0, 0, query_out,
+                                           static_cast<cudaStream_t>(stream)));
+}
+
+int tla_scores(tla_layer* L, const float* query, const int32_t* positions, float* scores_out, int32_t batch,
+               void* stream) {
+  if (!valid_layer(L) || !query || !positions || !scores_out || batch < 0 || batch > L->max_batch)
+    return TLA_ERR_INVALID_ARG;
+  if (batch == 0) return TLA_OK;
+  DeviceGuard g(L->ctx->device);
+  return from_cuda(tla::launch_scores(L, query, positions, batch, scores_out, static_cast<cudaStream_t>(stream)));
+}
+
+int tla_prefill(tla_layer* L, const void* qkv, const int32_t* start_pos, const void* gate, int32_t seq_len, void* out,
+                int32_t batch, void* stream) {
   if (!valid_layer(L) || !qkv || !start_pos || !out || batch < 0 || batch > L->max_batch || seq_len < 0 ||
       seq_len > L->max_tokens)
     return TLA_ERR_INVALID_ARG;
@@ -369,7 +445,7 @@ int tla_prefill(tla_layer* L, const void* qkv, const int32_t* start_pos, int32_t
   if (L->fast_prefill && !L->borrowed) {
     int rc = ensure_qscratch(L->ctx, static_cast<size_t>(batch) * seq_len * L->Hq * L->D * sizeof(__half));
     if (rc != TLA_OK) return rc;
-    return from_cuda(tla::launch_prefill_fast(L, qkv, start_pos, batch, seq_len, out, st));
+    return from_cuda(tla::launch_prefill_fast(L, qkv, start_pos, gate, batch, seq_len, out, st));
   }
   int rc = ensure_qscratch(L->ctx, static_cast<size_t>(batch) * seq_len * L->Hq * L->D * sizeof(float));
   if (rc != TLA_OK) return rc;
@@ -377,7 +453,7 @@ int tla_prefill(tla_layer* L, const void* qkv, const int32_t* start_pos, int32_t
   rc = from_cuda(tla::launch_rope_append(L, qkv, start_pos, batch, seq_len, 0, L->borrowed ? 0 : 1, qs, st));
   if (rc != TLA_OK) return rc;
   return from_cuda(
-      tla::launch_attend_generic(L, qs, start_pos, batch, seq_len, 0, L->max_tokens, nullptr, out, nullptr, st));
+      tla::launch_attend_generic(L, qs, start_pos, batch, seq_len, 0, L->max_tokens, gate, out, nullptr, st));
 }
 
 int tla_decode_partial(tla_layer* L, const void* qkv, const int32_t* positions, int32_t slot_offset,

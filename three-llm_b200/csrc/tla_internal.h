@@ -90,6 +90,14 @@ struct LayerArgs {
 
 LayerArgs layer_args(const tla_layer* L);
 
+// cudaFuncAttributeMaxDynamicSharedMemorySize is a property of a kernel
+// instance on the current device, shared by every layer that launches it:
+// raise it to `bytes` if it is lower, never lower it.
+cudaError_t raise_smem_limit(const void* kernel, int bytes);
+// Resident blocks per SM of a kernel instance at (threads, dynamic smem) on
+// the current device, cached per (device, kernel, threads, smem).
+cudaError_t cached_occupancy(const void* kernel, int threads, int smem, int* blocks);
+
 // Generic path (any head_dim <= 256, any GQA ratio, fp16 or fp32 cache).
 // rope_append: per (b, t) token at pos = start[b] + t: QK-norm + RoPE of Q into
 // qscr (float32 [B][S][Hq][D]); if append, K (norm + RoPE) and V (vNorm) into
@@ -101,6 +109,9 @@ cudaError_t launch_rope_append(const tla_layer* L, const void* qkv, const int32_
 cudaError_t launch_attend_generic(const tla_layer* L, const float* qscr, const int32_t* start, int batch,
                                   int seq_len, int slot_offset, int local_tokens, const void* gate, void* out,
                                   float* partial, cudaStream_t stream);
+// scaled scores of one decode step: scores[b][h][t] for t in [window start, pos[b]].
+cudaError_t launch_scores(const tla_layer* L, const float* query, const int32_t* positions, int batch, float* scores,
+                          cudaStream_t stream);
 // rope_append with the rotated queries written as fp16 [B][Hq][S][D] (fp16 cache only).
 cudaError_t launch_rope_append_half_q(const tla_layer* L, const void* qkv, const int32_t* start, int batch,
                                       int seq_len, __half* qscr, cudaStream_t stream);
@@ -125,7 +136,8 @@ cudaError_t launch_combine_lse(const float* partials, int ranks, int batch, int 
                                void* out, bool io_fp32, cudaStream_t stream);
 // Tensor-core prefill (tcgen05/TMEM/TMA), fp16 cache, D in {64, 128}.
 cudaError_t prefill_fast_configure(tla_layer* L);
-cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32_t* start, int batch, int seq_len,
-                                void* out, cudaStream_t stream);
+// gate: null or [batch][seq_len][Hq][D] in the layer's I/O type.
+cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32_t* start, const void* gate, int batch,
+                                int seq_len, void* out, cudaStream_t stream);
 
 }  // namespace tla
