@@ -46,6 +46,21 @@ def test_plans_cover_every_head_and_token_once(world):
     assert q == list(range(Hq)) and kv == list(range(Hk)) and toks == list(range(T))
 
 
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_batch_head_plan_covers_every_unit_once(world):
+    """Config 3's (sequence, KV-head group) units: 4 sequences x 2 KV heads over 1..8 ranks."""
+    sh = _sharding()
+    B, Hq, Hk = 4, 14, 2
+    units = []
+    for r in range(world):
+        s = sh.batch_head_shard(B, Hq, Hk, world, r)
+        assert s.q_count == s.kv_count * Hq // Hk and s.q_begin == s.kv_begin * Hq // Hk
+        units += [(b, k) for b in range(s.seq_begin, s.seq_begin + s.seq_count)
+                  for k in range(s.kv_begin, s.kv_begin + s.kv_count)]
+    assert sorted(units) == [(b, k) for b in range(B) for k in range(Hk)]
+    assert len(units) == len(set(units))
+
+
 def test_slice_qkv_for_heads():
     sh = _sharding()
     Hq, Hk, D, B = 8, 4, 3, 2

@@ -8,6 +8,9 @@ an exchange, plus the one place that needs one:
   groups (the contiguous GQA mapping floor(h*Hk/Hq), TSLAttention.ts:340), so
   its layer is just a smaller layer and its output stays head-sharded for a
   tensor-parallel output projection. No collective.
+- batch_head_shard: (sequence, KV-head group) units for batched prefill and
+  decode when there are more ranks than KV-head groups: KV-head part times
+  sequence part, again without a collective.
 - sequence_shard: rank r owns the contiguous token block
   [r*T/N, (r+1)*T/N); every rank emits (m, l, o) per query head with
   tla_decode_partial, and the triples meet either through one all-gather of
@@ -52,6 +55,33 @@ def slice_qkv_for_heads(qkv, shard, head_count, kv_head_count, head_dim):
     k = x[:, head_count + shard.kv_begin:head_count + shard.kv_begin + shard.kv_count]
     v = x[:, head_count + kv_head_count + shard.kv_begin:head_count + kv_head_count + shard.kv_begin + shard.kv_count]
     return torch.cat([q, k, v], dim=1).reshape(B, -1).contiguous()
+
+
+@dataclass(frozen=True)
+class BatchHeadShard:
+    seq_begin: int
+    seq_count: int
+    q_begin: int
+    q_count: int
+    kv_begin: int
+    kv_count: int
+
+
+def batch_head_shard(batch, head_count, kv_head_count, world, rank):
+    """Batched prefill / decode split over (sequence, KV-head group) units: the
+    KV heads are split over g = gcd(world, kv_head_count) rank groups and the
+    sequences over world / g, so rank r holds KV-head part r % g of sequences
+    part r // g (batch must divide by world / g). No exchange: every unit is a
+    smaller layer over its own sequences."""
+    import math
+
+    g = math.gcd(world, kv_head_count)
+    nb = world // g
+    if batch % nb or head_count % kv_head_count:
+        raise ValueError("the sequences must divide evenly over world / gcd(world, kv_head_count) ranks")
+    h = head_shard(head_count, kv_head_count, g, rank % g)
+    per = batch // nb
+    return BatchHeadShard((rank // g) * per, per, h.q_begin, h.q_count, h.kv_begin, h.kv_count)
 
 
 @dataclass(frozen=True)
