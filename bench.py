@@ -863,6 +863,17 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------- main
+def guarded(fn, *a, **kw):
+    """A sub-record that fails is reported in the line instead of losing it."""
+    try:
+        return fn(*a, **kw)
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        traceback.print_exc()
+        return {"error": f"{type(e).__name__}: {e}"}
+
+
 def sub_decode(name, cls, pkg, torch, device, rank, world, args, hbm, parity=True, **kw):
     wl = cls(pkg, torch, device, rank, world, args, **kw)
     try:
@@ -979,19 +990,21 @@ def main():
     if args.workload == "decode_1b" and not args.headline_only:
         sweep = {}
         for b in (1, 8, 32):
-            sweep[str(b)] = sub_decode("decode_1b", Decode1B, pkg, torch, device, rank, world, args, hbm,
-                                       parity=False, batch=b)
+            sweep[str(b)] = guarded(sub_decode, "decode_1b", Decode1B, pkg, torch, device, rank, world, args, hbm,
+                                    parity=False, batch=b)
         line["decode_1b_batch"] = sweep
-        line["ragged_8b"] = sub_decode("ragged_8b", Ragged8B, pkg, torch, device, rank, world, args, hbm)
-        line["long_ctx_heads"] = sub_decode("long_ctx_heads", LongCtxHeads, pkg, torch, device, rank, world, args, hbm)
+        line["ragged_8b"] = guarded(sub_decode, "ragged_8b", Ragged8B, pkg, torch, device, rank, world, args, hbm)
+        line["long_ctx_heads"] = guarded(sub_decode, "long_ctx_heads", LongCtxHeads, pkg, torch, device, rank, world,
+                                         args, hbm)
         if world > 1:
-            line["long_ctx_seq"] = sub_decode("long_ctx_seq", LongCtxSeq, pkg, torch, device, rank, world, args, hbm)
+            line["long_ctx_seq"] = guarded(sub_decode, "long_ctx_seq", LongCtxSeq, pkg, torch, device, rank, world,
+                                           args, hbm)
         else:
             line["long_ctx_seq"] = dict(line["long_ctx_heads"], note="one GPU holds every token block: the plain "
                                                                      "decode of long_ctx_heads")
-        line["prefill"] = run_prefill(pkg, torch, device, rank, world, args, tc, src)
-        for key in ("ragged_8b", "long_ctx_heads", "long_ctx_seq", "prefill"):
-            line[key]["workload"] = line[key].get("workload", WORKLOAD_LABELS["long_ctx" if "long" in key else key])
+        line["prefill"] = guarded(run_prefill, pkg, torch, device, rank, world, args, tc, src)
+        for key in ("ragged_8b", "long_ctx_heads", "long_ctx_seq"):
+            line[key].setdefault("workload", WORKLOAD_LABELS["long_ctx" if key.startswith("long") else key])
     if rank == 0:
         checks = [line.get("parity")] + [line.get(k, {}).get("parity") for k in
                                          ("ragged_8b", "long_ctx_heads", "long_ctx_seq", "prefill")]
