@@ -175,6 +175,35 @@ int tla_scores(tla_layer* layer, const float* query, const int32_t* positions, f
 int tla_prefill(tla_layer* layer, const void* qkv, const int32_t* start_pos, const void* gate, int32_t seq_len,
                 void* out, int32_t batch, void* stream);
 
+/* The QKV projection feeding this layer (TSLLinear, packages/three-llm/src/tsl/TSLLinear.ts:56-75,
+ * wired at decoder/DecoderTSLRunner.ts:293-297; CPU linear, runtime/math.ts:6-25), fused with the
+ * attention's front end: [Q | K | V] = x W + bias runs on the tensor cores and its epilogue applies the
+ * QK-norm and RoPE at each row's position, appends K and V (vNorm) to the cache and hands the rotated
+ * queries to the attention kernel, so the raw [Q | K | V] rows never go through HBM. The result equals
+ * tla_decode / tla_prefill on qkv = x W + bias.
+ *   x      device fp16 [batch][hidden] (decode) or [batch][seq_len][hidden] (prefill)
+ *   weight device fp16 [hidden][(head_count + 2*kv_head_count) * head_dim]: the reference's
+ *          [inputSize][outputSize] layout
+ *   bias   device float32 [(head_count + 2*kv_head_count) * head_dim] or NULL
+ * hidden must be a multiple of 8; fp16 I/O and cache, head_dim 64 or 128 (else TLA_ERR_UNSUPPORTED). */
+int tla_qkv_decode(tla_layer* layer, const void* x, const void* weight, const float* bias, int32_t hidden,
+                   const int32_t* positions, const void* gate, void* out, int32_t batch, void* stream);
+int tla_qkv_prefill(tla_layer* layer, const void* x, const void* weight, const float* bias, int32_t hidden,
+                    const int32_t* start_pos, const void* gate, int32_t seq_len, void* out, int32_t batch,
+                    void* stream);
+
+/* The attention output projection and the residual add after it (DecoderTSLRunner.ts:299-309, 353-356:
+ * attnProj TSLLinear, then TSLAdd): y = residual + attn W + bias on the tensor cores.
+ *   attn     device fp16 [rows][in_features] (attention output rows)
+ *   weight   device fp16 [in_features][hidden] (the reference's [inputSize][outputSize] layout)
+ *   bias     device float32 [hidden] or NULL; residual device [rows][hidden] or NULL
+ *   y        device [rows][hidden]
+ * With TLA_FLAG_IO_FP32 in io_flags, residual and y are float32 (else fp16). in_features and hidden
+ * must be multiples of 64. With head-sharded attention, the rank's attention columns and the matching
+ * rows of W give this rank's partial product (bias and residual NULL, float32 y), which the ranks sum. */
+int tla_out_proj(tla_ctx* ctx, const void* attn, const void* weight, const float* bias, const void* residual,
+                 void* y, int32_t rows, int32_t in_features, int32_t hidden, uint32_t io_flags, void* stream);
+
 /* Sequence-sharded decode building block: attend over cache slots
  * [0, local_tokens) that hold global positions [slot_offset, slot_offset +
  * local_tokens), and emit per query head the partial triple

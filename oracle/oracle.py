@@ -93,6 +93,7 @@ def lib():
         L.orc_decode_batch.argtypes = [P, P, i32, i32, P, P, P, P, P, i32]
         L.orc_prefill.argtypes = [P, P, P, i32, i32, i32, P, P, P, P, i32]
         L.orc_attend_heads.argtypes = [P, P, i32, i32, P, P, P, i32, i32, P, i32]
+        L.orc_linear.argtypes = [P, i32, P, P, i32, i32, P, i32]
         _lib = L
     return _lib
 
@@ -247,6 +248,18 @@ def attend_heads(q_rot, positions, key_cache, value_cache, head_begin, head_end,
     _check(lib().orc_attend_heads(_ptr(q), _ptr(pos), B, T, _ptr(key_cache), _ptr(value_cache), ctypes.byref(o),
                                   int(head_begin), int(head_end), _ptr(out), int(threads)))
     return out
+
+
+def linear(x, weight, bias=None, threads=1):
+    """linear (math.ts:6-25): x [..., in] @ weight [in, out] + bias, double sums, float32 result."""
+    x = _f32(x)
+    w = _f32(weight)
+    b = None if bias is None else _f32(bias)
+    lead = x.shape[:-1]
+    rows = int(np.prod(lead)) if lead else 1
+    out = np.zeros((rows, w.shape[1]), dtype=np.float32)
+    _check(lib().orc_linear(_ptr(x), rows, _ptr(w), _ptr(b), w.shape[0], w.shape[1], _ptr(out), int(threads)))
+    return out.reshape(*lead, w.shape[1])
 
 
 def fill_sin(n, seed):

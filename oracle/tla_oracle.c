@@ -329,6 +329,27 @@ int orc_prefill(const float* qkv, const int32_t* start_pos, const float* gate, i
   return rc;
 }
 
+int orc_linear(const float* input, int32_t rows, const float* weight, const float* bias, int32_t in_size,
+               int32_t out_size, float* target, int32_t threads) {
+  if (!input || !weight || !target || rows < 0 || in_size <= 0 || out_size <= 0) return ORC_ERR_ARG;
+  set_threads(threads);
+#pragma omp parallel for schedule(static) if (threads > 1)
+  for (int32_t r = 0; r < rows; r++) {
+    const float* x = input + (size_t)r * in_size;
+    float* y = target + (size_t)r * out_size;
+    double* sum = (double*)malloc(sizeof(double) * (size_t)out_size);
+    for (int32_t o = 0; o < out_size; o++) sum[o] = bias ? (double)bias[o] : 0;   /* math.ts:15 */
+    for (int32_t i = 0; i < in_size; i++) {                                        /* math.ts:17-19 */
+      const double xi = (double)x[i];
+      const float* w = weight + (size_t)i * out_size;
+      for (int32_t o = 0; o < out_size; o++) sum[o] += xi * (double)w[o];
+    }
+    for (int32_t o = 0; o < out_size; o++) y[o] = (float)sum[o];                  /* :21, Float32Array store */
+    free(sum);
+  }
+  return ORC_OK;
+}
+
 int orc_attend_heads(const float* q_rot, const int32_t* positions, int32_t batch, int32_t max_tokens,
                      const float* key_cache, const float* value_cache, const orc_attn_options* o,
                      int32_t head_begin, int32_t head_end, float* out, int32_t threads) {

@@ -118,6 +118,13 @@ int orc_prefill(const float* qkv, const int32_t* start_pos, const float* gate, i
                 int32_t max_tokens, float* key_cache, float* value_cache, const orc_attn_options* o,
                 float* out, int32_t threads);
 
+/* linear (packages/three-llm/src/runtime/math.ts:6-25) for `rows` independent
+ * inputs: target[r][o] = bias[o] + sum_i input[r][i] * weight[i][o], the sum in
+ * double (JS numbers), the result stored as float32. weight is the reference's
+ * [inputSize][outputSize] layout; bias may be NULL. Rows run on `threads`. */
+int orc_linear(const float* input, int32_t rows, const float* weight, const float* bias, int32_t in_size,
+               int32_t out_size, float* target, int32_t threads);
+
 /* Attention of the listed query heads only, over an already-filled cache
  * (no append): used to time a bounded sample of a large decode workload.
  * q_rot: post-RoPE queries [B][Hq*D]. */

@@ -101,6 +101,8 @@ struct DecodeParams {
   const void* gate;
   void* out;
   float* partial_out;  // sequence-shard mode: [B][Hq][D + 2]; null => out
+  const __half* qrot;  // null, or the rotated queries [B][Hq][D] fp16 from the fused QKV projection
+                       // (which also appended the new K/V): no QK-norm / RoPE / append here
   float* scratch;      // [grid][2][G][D + 2]
   int32_t* counters;   // [B * Hk], zero between launches
   int batch, slot_offset, local_tokens, append;
@@ -284,6 +286,11 @@ __device__ __forceinline__ void prefetch_first_rows(const DecodeParams& p, const
   int b = 0;
   while (prefix[b + 1] <= tb) ++b;
   const int kvh = seg_at(prefix, b, a.Hk, Units<D>::kSetup, tb, te).kvh;
+  if (p.qrot != nullptr) {  // the group's rotated query rows only
+    const char* q = reinterpret_cast<const char*>(p.qrot + (static_cast<size_t>(b) * a.Hq + kvh * a.G) * D);
+    if (tid < a.G * D * 2 / 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(q + tid * 128));
+    return;
+  }
   const char* row = static_cast<const char*>(p.qkv) + static_cast<size_t>(b) * (a.Hq + 2 * a.Hk) * D * sizeof(IO);
   constexpr int kRowLines = D * sizeof(IO) / 128;  // 128-byte lines per head row (D * sizeof(IO) >= 128)
   const int q_lines = a.G * kRowLines;
@@ -455,7 +462,8 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     const int slot_new = pos - p.slot_offset;
     if (tid == 0 && it == 0) DTRACE_AFTER(15, pos);
     const bool has_new = p.append && (lt + n == tiles);
-    const IO* row = qkv + static_cast<size_t>(b) * row_stride;
+    const bool qready = p.qrot != nullptr;
+    const IO* row = qready ? nullptr : qkv + static_cast<size_t>(b) * row_stride;
 
     // ---- segment setup: QK-norm + RoPE of the group's queries (and the new K/V)
     // All global loads of the set-up go out together (read-only path) before
@@ -464,10 +472,20 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     {
       constexpr int kQPer = 16 * D / 128;  // elements per thread for up to 16 query rows
       float qv[kQPer];
+      if (qready) {
+        const __half* qr = p.qrot + (static_cast<size_t>(b) * Hq + kvh * G) * D;
 #pragma unroll
-      for (int u = 0; u < kQPer; ++u) {
-        const int i = tid + 128 * u;
-        qv[u] = i < G * D ? to_f32(__ldg(row + kvh * G * D + i)) : 0.f;
+        for (int u = 0; u < kQPer; ++u) {
+          const int i = tid + 128 * u;
+          qv[u] = i < G * D ? __half2float(qr[i]) : 0.f;
+        }
+      } else {
+        const IO* qsrc = row + kvh * G * D;
+#pragma unroll
+        for (int u = 0; u < kQPer; ++u) {
+          const int i = tid + 128 * u;
+          qv[u] = i < G * D ? to_f32(__ldg(qsrc + i)) : 0.f;
+        }
       }
       float kv0 = 0.f, kv1 = 0.f, kv2 = 0.f, kv3 = 0.f;  // the new K/V: D <= 256 values each
       if (has_new && (D >= 128 || tid < D)) {  // (at D = 64 a wider read would run past the last V row)
@@ -509,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       const float* w;
       float* v;
       if (h < G) {
-        if (a.q_norm == nullptr) continue;
+        if (a.q_norm == nullptr || qready) continue;
         w = a.q_norm;
         v = qf + h * D;
       } else if (h == G) {
@@ -546,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     };
     for (int i = tid; i < G * D; i += 128) {  // rows G..15 were zeroed at the start
       const int r = i / D, d = i - r * D;
-      q_s[r * (C::kQPitch / 2) + d] = __float2half_rn(rope(qf + r * D, d));
+      q_s[r * (C::kQPitch / 2) + d] = __float2half_rn(qready ? qf[r * D + d] : rope(qf + r * D, d));
     }
     if (has_new)
       for (int d = tid; d < D; d += 128) {
@@ -1285,6 +1303,7 @@ DecodeParams decode_params(const tla_layer* L, const void* qkv, const int32_t* p
   p.tmap_v = L->tmap_v;
   p.a = layer_args(L);
   p.qkv = qkv;
+  p.qrot = nullptr;
   p.positions = positions;
   p.gate = gate;
   p.out = out;
@@ -1306,6 +1325,13 @@ cudaError_t launch_decode_fast(const tla_layer* L, const void* qkv, const int32_
                                void* out, float* partial, int batch, int slot_offset, int local_tokens, int append,
                                cudaStream_t stream) {
   const DecodeParams p = decode_params(L, qkv, positions, gate, out, partial, batch, slot_offset, local_tokens, append);
+  return L->D == 64 ? dispatch_launch<64>(L, p, nullptr, stream) : dispatch_launch<128>(L, p, nullptr, stream);
+}
+
+cudaError_t launch_decode_fast_qrot(const tla_layer* L, const __half* qrot, const int32_t* positions, const void* gate,
+                                    void* out, int batch, cudaStream_t stream) {
+  DecodeParams p = decode_params(L, nullptr, positions, gate, out, nullptr, batch, 0, L->max_tokens, 0);
+  p.qrot = qrot;
   return L->D == 64 ? dispatch_launch<64>(L, p, nullptr, stream) : dispatch_launch<128>(L, p, nullptr, stream);
 }
 

@@ -1,0 +1,380 @@
+// Dense projections on the 5th-generation tensor cores (tcgen05): fp16
+// operands fed by TMA, fp32 accumulation in TMEM, with the attention's front
+// and back ends fused into the epilogue.
+//
+//  - QKV projection (TSLLinear, packages/three-llm/src/tsl/TSLLinear.ts:56-75;
+//    CPU linear, runtime/math.ts:6-25; wired at decoder/DecoderTSLRunner.ts:
+//    293-297): [Q | K | V] = x W + bias, then per head the QK-norm and RoPE
+//    at the row's position (TSLAttention.ts:168-304), K and V (vNorm)
+//    appended to the cache (copy-KV, :252-286) and the rotated queries handed
+//    to the attention kernel, so the raw [Q | K | V] rows never reach HBM.
+//  - Output projection and residual (DecoderTSLRunner.ts:299-309, 353-356:
+//    the attnProj TSLLinear, then TSLAdd): y = residual + attn W_o + bias, or
+//    one rank's fp32 partial product when the heads are sharded.
+//
+// Tile: 128 rows (the TMEM lanes) x NT columns (64..256; whole heads for the
+// QKV epilogue), the reduction dimension in 64-element stages. Warp 0 lane 0
+// issues the TMA loads of x (K-major, 128-byte swizzle) and W (stored
+// [in][out], i.e. MN-major for the MMA's B operand, in 64-column boxes) into a
+// ring of shared-memory stages; warp 1 owns TMEM and its lane 0 issues
+// tcgen05.mma (M = 128, N = NT, K = 16) per stage and commits the stage back
+// to the producer; then all four warps run the epilogue, thread = row = TMEM
+// lane. Every mbarrier wait is bounded (TLA_ERR_TIMEOUT).
+#include <math.h>
+
+#include "tcgen05.cuh"
+#include "tla_device.cuh"
+#include "tla_internal.h"
+
+namespace tla {
+
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kXStage = 128 * 128;  // x: 128 rows x 64 fp16 (one 128-byte row each)
+constexpr int kWBox = 64 * 128;     // W: 64 rows of the reduction dim x 64 fp16 columns
+enum : int { kQkvDecode = 0, kQkvPrefill = 1, kOutProj = 2 };
+
+struct ProjParams {
+  CUtensorMap tm_x;  // [rows][K] fp16, box {64, 128}
+  CUtensorMap tm_w;  // [K][N] fp16, box {64, 64}
+  int rows, K, N, NT, stages, m_tiles;
+  uint32_t tmem_cols;
+  int mode;
+  const float* bias;  // [N] or null
+  int* error;
+  // QKV modes
+  LayerArgs a;
+  const int32_t* pos;  // decode: positions [B]; prefill: start positions [B]
+  int S;               // prefill: tokens per sequence
+  __half* qout;        // decode: [B][Hq][D]; prefill: [B][Hq][S][D] (the prefill kernel's TMA source)
+  // output projection
+  const void* residual;  // [rows][N] or null
+  void* y;               // [rows][N]
+  int y_f32, res_f32;    // float32 (else fp16) output / residual
+};
+
+__host__ __device__ inline int stage_bytes(int NT) { return kXStage + (NT / 64) * kWBox; }
+
+template <int D>
+__host__ __device__ inline int epilogue_bytes(int mode) {
+  return mode == kOutProj ? 0 : 2 * kThreads * (D + 1) * 4;  // each row's head values and its cos / sin
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_constant__ ProjParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int sb = stage_bytes(p.NT);
+  const int ring = p.stages * sb, epi = epilogue_bytes<D>(p.mode);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (ring > epi ? ring : epi));
+  uint64_t* empty = full + p.stages;
+  uint64_t* accb = empty + p.stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m0 = (static_cast<int>(blockIdx.x) % p.m_tiles) * 128;
+  const int n0 = (static_cast<int>(blockIdx.x) / p.m_tiles) * p.NT;
+  const int kchunks = (p.K + 63) / 64;
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(p.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // x, positions and the residual may come from the previous kernel
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    if (*abort_flag) return;
+    if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
+  };
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    tma_prefetch(&p.tm_x);
+    tma_prefetch(&p.tm_w);
+    for (int c = 0; c < kchunks; ++c) {
+      const int s = c % p.stages;
+      wait(&empty[s], ((c / p.stages) & 1) ^ 1);
+      if (*abort_flag) continue;
+      uint8_t* st = smem + s * sb;
+      mbar_arrive_expect_tx(&full[s], sb);
+      tma_load_2d(st, &p.tm_x, &full[s], c * 64, m0);
+      for (int i = 0; i < p.NT / 64; ++i) tma_load_2d(st + kXStage + i * kWBox, &p.tm_w, &full[s], n0 + 64 * i, c * 64);
+    }
+    for (int c = kchunks > p.stages ? kchunks - p.stages : 0; c < kchunks; ++c)  // no copies in flight at exit
+      wait(&full[c % p.stages], (c / p.stages) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer
+    const uint32_t idesc = idesc_f16(128, p.NT, true);
+    // Descriptors are linear in the start address (no carry below 256 KB):
+    // stage and k-step offsets are plain adds. x: K-major, 32 bytes per k-step;
+    // W: MN-major, 64-column boxes kWBox apart, 16 rows (2048 bytes) per k-step.
+    const uint64_t dx = sdesc(smem_u32(smem), 16, 1024);
+    const uint64_t dw = sdesc(smem_u32(smem + kXStage), kWBox, 1024);
+    for (int c = 0; c < kchunks; ++c) {
+      const int s = c % p.stages;
+      wait(&full[s], (c / p.stages) & 1);
+      tc_fence_after();
+      if (!*abort_flag) {
+        const uint64_t so = static_cast<uint64_t>((s * sb) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) mma_f16(tmem, dx + so + kk * 2, dw + so + kk * 128, idesc, (c | kk) ? 1u : 0u);
+      }
+      mma_commit(&empty[s]);
+    }
+    mma_commit(accb);
+  }
+  __syncwarp();
+  wait(accb, 0);
+  __syncwarp();
+  tc_fence_after();
+
+  const int r = tid, row = m0 + r;
+  const bool valid = row < p.rows;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  if (p.mode != kOutProj) {
+    // ---------------------------------------------------------------- QKV epilogue
+    const LayerArgs& a = p.a;
+    int b = 0, t = 0, pos = -1;
+    if (valid) {
+      if (p.mode == kQkvDecode) {
+        b = row;
+        pos = p.pos[row];
+      } else {
+        b = row / p.S;
+        t = row - b * p.S;
+        pos = p.pos[b] + t;
+      }
+    }
+    const bool ok = valid && pos >= 0 && pos < a.max_tokens;
+    if (valid && !ok && n0 == 0) report_error(a.error, TLA_ERR_POSITION);  // the row is skipped
+    float* hrow = reinterpret_cast<float*>(smem) + r * (D + 1);                   // padded: no bank conflicts
+    float* cs = reinterpret_cast<float*>(smem) + kThreads * (D + 1) + r * (D + 1);  // cos [half], sin [half]
+    const int half = a.rotary / 2;
+    const int head0 = n0 / D, heads = p.NT / D;
+    if (ok && half > 0 && head0 < a.Hq + a.Hk)  // the tile holds a Q or K head: this row's RoPE factors
+      for (int i = 0; i < half; ++i) {
+        float c = 1.f, s = 0.f;
+        if (i < a.pair_count) rope_cos_sin(pos, __ldg(a.inv_freq + i), &c, &s);
+        cs[i] = c;
+        cs[half + i] = s;
+      }
+    for (int j = 0; j < heads; ++j) {
+      const int hh = head0 + j;
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tmem_ld32(lane_base + j * D + 32 * c, v);  // warp-collective: every lane loads
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x = v[i] + (p.bias ? __ldg(p.bias + hh * D + 32 * c + i) : 0.f);
+          hrow[32 * c + i] = x;
+          ss += x * x;
+        }
+      }
+      if (!ok) continue;
+      const bool isq = hh < a.Hq, isk = !isq && hh < a.Hq + a.Hk;
+      const float* w = isq ? a.q_norm : (isk ? a.k_norm : nullptr);
+      const bool norm = (isq || isk) ? w != nullptr : a.v_norm != 0;  // rmsNormPackedHeads, math.ts:154-167
+      const float inv = norm ? 1.f / sqrtf(ss / static_cast<float>(D) + a.rms_eps) : 1.f;
+      auto val = [&](int d) -> float {
+        float x = hrow[d] * inv;
+        if (w) x *= a.offset_rms ? 1.f + __ldg(w + d) : __ldg(w + d);
+        return x;
+      };
+      __half* dst;
+      if (isq)
+        dst = p.qout + (p.mode == kQkvDecode ? (static_cast<size_t>(b) * a.Hq + hh) * D
+                                             : ((static_cast<size_t>(b) * a.Hq + hh) * p.S + t) * D);
+      else if (isk)
+        dst = static_cast<__half*>(a.k_cache) +
+              ((static_cast<size_t>(b) * a.Hk + (hh - a.Hq)) * a.max_tokens + pos) * D;
+      else
+        dst = static_cast<__half*>(a.v_cache) +
+              ((static_cast<size_t>(b) * a.Hk + (hh - a.Hq - a.Hk)) * a.max_tokens + pos) * D;
+      const bool rope = (isq || isk) && half > 0;
+      for (int d0 = 0; d0 < D; d0 += 8) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          float y[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int d = d0 + e + u;
+            float x = val(d);
+            if (rope && d < a.rotary) {  // rotate-half RoPE, math.ts:134-147
+              const int jj = d < half ? d : d - half;
+              if (jj < a.pair_count) {
+                const float partner = d < half ? -val(d + half) : val(d - half);
+                x = (x * cs[jj] + partner * cs[half + jj]) * a.attn_factor;
+              }
+            }
+            y[u] = x;
+          }
+          pk[e / 2] = pack_half2(y[0], y[1]);
+        }
+        *reinterpret_cast<uint4*>(dst + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- output projection epilogue
+    for (int c = 0; c < p.NT / 32; ++c) {
+      float v[32];
+      tmem_ld32(lane_base + 32 * c, v);
+      if (!valid) continue;
+      const int col = n0 + 32 * c;
+      const size_t o = static_cast<size_t>(row) * p.N + col;
+      if (p.bias) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += __ldg(p.bias + col + i);
+      }
+      if (p.residual) {
+        if (p.res_f32) {
+          const float4* res = reinterpret_cast<const float4*>(static_cast<const float*>(p.residual) + o);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 q = res[i];
+            v[4 * i] += q.x;
+            v[4 * i + 1] += q.y;
+            v[4 * i + 2] += q.z;
+            v[4 * i + 3] += q.w;
+          }
+        } else {
+          const uint4* res = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.residual) + o);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 q = res[i];
+            const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              v[8 * i + 2 * k] += __low2float(h[k]);
+              v[8 * i + 2 * k + 1] += __high2float(h[k]);
+            }
+          }
+        }
+      }
+      if (p.y_f32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.y) + o);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.y) + o);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(pack_half2(v[8 * i], v[8 * i + 1]), pack_half2(v[8 * i + 2], v[8 * i + 3]),
+                              pack_half2(v[8 * i + 4], v[8 * i + 5]), pack_half2(v[8 * i + 6], v[8 * i + 7]));
+      }
+    }
+  }
+  griddep_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
+  }
+}
+
+CUresult make_map_2d(const tla_ctx* ctx, const void* base, uint64_t inner, uint64_t outer, uint32_t box_outer,
+                     CUtensorMap* map) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint32_t box[2] = {64, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+// Widest tile (<= 256 columns, a multiple of `unit` dividing N) that still gives
+// every SM a tile; the narrowest if none does (few rows: decode).
+int choose_nt(int N, int unit, int m_tiles, int sms) {
+  int best = 0;
+  for (int nt = unit; nt <= 256; nt += unit) {
+    if (N % nt) continue;
+    if (best == 0 || static_cast<long long>(m_tiles) * (N / nt) >= sms) best = nt;
+  }
+  return best;
+}
+
+template <int D>
+cudaError_t launch_proj_t(const tla_ctx* ctx, ProjParams& p, cudaStream_t stream) {
+  const int sb = stage_bytes(p.NT);
+  int stages = (200 * 1024) / sb;
+  if (stages > 8) stages = 8;
+  if (stages < 2) stages = 2;
+  p.stages = stages;
+  p.tmem_cols = p.NT <= 64 ? 64 : (p.NT <= 128 ? 128 : 256);
+  const int ring = stages * sb, epi = epilogue_bytes<D>(p.mode);
+  const int smem = (ring > epi ? ring : epi) + (2 * stages + 1) * 8 + 16 + 1024;
+  const void* k = reinterpret_cast<const void*>(proj_tc_kernel<D>);
+  cudaError_t e = raise_smem_limit(k, smem);
+  if (e != cudaSuccess) return e;
+  const int n_tiles = p.N / p.NT;
+  return launch_pdl(proj_tc_kernel<D>, static_cast<unsigned>(p.m_tiles * n_tiles), kThreads, smem, stream, p);
+}
+
+}  // namespace
+
+cudaError_t launch_qkv_proj(const tla_layer* L, const void* x, const void* weight, const float* bias, int hidden,
+                            const int32_t* pos, int rows, int seq_len, bool prefill, __half* qout,
+                            cudaStream_t stream) {
+  ProjParams p{};
+  const int N = (L->Hq + 2 * L->Hk) * L->D;
+  if (make_map_2d(L->ctx, x, hidden, rows, 128, &p.tm_x) != CUDA_SUCCESS ||
+      make_map_2d(L->ctx, weight, N, hidden, 64, &p.tm_w) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  p.rows = rows;
+  p.K = hidden;
+  p.N = N;
+  p.m_tiles = (rows + 127) / 128;
+  p.NT = choose_nt(N, L->D, p.m_tiles, L->ctx->sm_count);
+  if (p.NT == 0) return cudaErrorInvalidValue;
+  p.mode = prefill ? kQkvPrefill : kQkvDecode;
+  p.bias = bias;
+  p.error = L->ctx->d_error;
+  p.a = layer_args(L);
+  p.pos = pos;
+  p.S = seq_len;
+  p.qout = qout;
+  return L->D == 64 ? launch_proj_t<64>(L->ctx, p, stream) : launch_proj_t<128>(L->ctx, p, stream);
+}
+
+cudaError_t launch_out_proj(const tla_ctx* ctx, const void* attn, const void* weight, const float* bias,
+                            const void* residual, bool residual_f32, void* y, bool y_f32, int rows, int in_features,
+                            int hidden, cudaStream_t stream) {
+  ProjParams p{};
+  if (make_map_2d(ctx, attn, in_features, rows, 128, &p.tm_x) != CUDA_SUCCESS ||
+      make_map_2d(ctx, weight, hidden, in_features, 64, &p.tm_w) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  p.rows = rows;
+  p.K = in_features;
+  p.N = hidden;
+  p.m_tiles = (rows + 127) / 128;
+  p.NT = choose_nt(hidden, 64, p.m_tiles, ctx->sm_count);
+  if (p.NT == 0) return cudaErrorInvalidValue;
+  p.mode = kOutProj;
+  p.bias = bias;
+  p.error = ctx->d_error;
+  p.residual = residual;
+  p.res_f32 = residual_f32 ? 1 : 0;
+  p.y = y;
+  p.y_f32 = y_f32 ? 1 : 0;
+  return launch_proj_t<64>(ctx, p, stream);
+}
+
+}  // namespace tla

@@ -456,6 +456,56 @@ int tla_prefill(tla_layer* L, const void* qkv, const int32_t* start_pos, const v
       tla::launch_attend_generic(L, qs, start_pos, batch, seq_len, 0, L->max_tokens, gate, out, nullptr, st));
 }
 
+int tla_qkv_decode(tla_layer* L, const void* x, const void* weight, const float* bias, int32_t hidden,
+                   const int32_t* positions, const void* gate, void* out, int32_t batch, void* stream) {
+  if (!valid_layer(L) || !x || !weight || !positions || !out || batch < 0 || batch > L->max_batch || hidden <= 0 ||
+      hidden % 8 != 0)
+    return TLA_ERR_INVALID_ARG;
+  if (!L->fast_decode || L->io_fp32 || L->cache_fp32) return TLA_ERR_UNSUPPORTED;
+  if (L->borrowed) return TLA_ERR_SHARED;
+  if (batch == 0) return TLA_OK;
+  DeviceGuard g(L->ctx->device);
+  int rc = ensure_qscratch(L->ctx, static_cast<size_t>(batch) * L->Hq * L->D * sizeof(__half));
+  if (rc != TLA_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  __half* q = static_cast<__half*>(L->ctx->d_qscratch);
+  rc = from_cuda(tla::launch_qkv_proj(L, x, weight, bias, hidden, positions, batch, 1, false, q, st));
+  if (rc != TLA_OK) return rc;
+  return from_cuda(tla::launch_decode_fast_qrot(L, q, positions, gate, out, batch, st));
+}
+
+int tla_qkv_prefill(tla_layer* L, const void* x, const void* weight, const float* bias, int32_t hidden,
+                    const int32_t* start_pos, const void* gate, int32_t seq_len, void* out, int32_t batch,
+                    void* stream) {
+  if (!valid_layer(L) || !x || !weight || !start_pos || !out || batch < 0 || batch > L->max_batch || seq_len < 0 ||
+      seq_len > L->max_tokens || hidden <= 0 || hidden % 8 != 0)
+    return TLA_ERR_INVALID_ARG;
+  if (!L->fast_prefill || L->io_fp32 || L->cache_fp32) return TLA_ERR_UNSUPPORTED;
+  if (L->borrowed) return TLA_ERR_SHARED;
+  if (batch == 0 || seq_len == 0) return TLA_OK;
+  DeviceGuard g(L->ctx->device);
+  int rc = ensure_qscratch(L->ctx, static_cast<size_t>(batch) * seq_len * L->Hq * L->D * sizeof(__half));
+  if (rc != TLA_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  __half* q = static_cast<__half*>(L->ctx->d_qscratch);
+  rc = from_cuda(tla::launch_qkv_proj(L, x, weight, bias, hidden, start_pos, batch * seq_len, seq_len, true, q, st));
+  if (rc != TLA_OK) return rc;
+  return from_cuda(tla::launch_prefill_attention(L, start_pos, gate, batch, seq_len, out, st));
+}
+
+int tla_out_proj(tla_ctx* ctx, const void* attn, const void* weight, const float* bias, const void* residual, void* y,
+                 int32_t rows, int32_t in_features, int32_t hidden, uint32_t io_flags, void* stream) {
+  if (!ctx || !attn || !weight || !y || rows < 0 || in_features <= 0 || hidden <= 0 || in_features % 64 != 0 ||
+      hidden % 64 != 0)
+    return TLA_ERR_INVALID_ARG;
+  if (ctx->encode_tiled == nullptr) return TLA_ERR_UNSUPPORTED;
+  if (rows == 0) return TLA_OK;
+  DeviceGuard g(ctx->device);
+  const bool f32 = (io_flags & TLA_FLAG_IO_FP32) != 0;
+  return from_cuda(tla::launch_out_proj(ctx, attn, weight, bias, residual, f32, y, f32, rows, in_features, hidden,
+                                        static_cast<cudaStream_t>(stream)));
+}
+
 int tla_decode_partial(tla_layer* L, const void* qkv, const int32_t* positions, int32_t slot_offset,
                        int32_t local_tokens, int32_t append, float* partial, int32_t batch, void* stream) {
   if (!valid_layer(L) || !qkv || !positions || !partial || batch < 0 || batch > L->max_batch || slot_offset < 0 ||

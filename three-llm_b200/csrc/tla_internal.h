@@ -140,4 +140,23 @@ cudaError_t prefill_fast_configure(tla_layer* L);
 cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32_t* start, const void* gate, int batch,
                                 int seq_len, void* out, cudaStream_t stream);
 
+// The causal attention kernel alone, over rotated queries already in the
+// context's query scratch ([B][Hq][S][D] fp16) and K/V already appended.
+cudaError_t launch_prefill_attention(const tla_layer* L, const int32_t* start, const void* gate, int batch,
+                                     int seq_len, void* out, cudaStream_t stream);
+// Decode over rotated queries [B][Hq][D] fp16 whose new K/V rows are already
+// in the cache (the fused QKV projection's output).
+cudaError_t launch_decode_fast_qrot(const tla_layer* L, const __half* qrot, const int32_t* positions,
+                                    const void* gate, void* out, int batch, cudaStream_t stream);
+// Tensor-core projections (proj_tc.cu). QKV: x [rows][hidden] fp16 times
+// weight [hidden][(Hq+2Hk)D] fp16 (+ bias), epilogue QK-norm / RoPE / append,
+// rotated queries to qout. Output projection: y = residual + attn W + bias
+// (or the bare product with y float32 and no residual / bias).
+cudaError_t launch_qkv_proj(const tla_layer* L, const void* x, const void* weight, const float* bias, int hidden,
+                            const int32_t* pos, int rows, int seq_len, bool prefill, __half* qout,
+                            cudaStream_t stream);
+cudaError_t launch_out_proj(const tla_ctx* ctx, const void* attn, const void* weight, const float* bias,
+                            const void* residual, bool residual_f32, void* y, bool y_f32, int rows, int in_features,
+                            int hidden, cudaStream_t stream);
+
 }  // namespace tla
