@@ -732,6 +732,258 @@ def run_prefill(pkg, torch, device, rank, world, args, tc, src, cpu=True):
     return rec
 
 
+# ---------------------------------------------------------------- projections around the attention
+HIDDEN_1B, HIDDEN_05B, HIDDEN_8B = 2048, 896, 4096
+
+
+class QkvDecode1B(Decode1B):
+    """Config 2 with the QKV projection in front (Llama-3.2-1B shapes: hidden
+    2048): every layer is one tla_qkv_decode, the tcgen05 projection whose
+    epilogue does QK-norm / RoPE / append, then the decode kernel."""
+
+    name = "qkv_decode_1b"
+
+    def __init__(self, pkg, torch, device, rank, world, args):
+        super().__init__(pkg, torch, device, rank, world, args)
+        Hq, Hk, D = DECODE_1B["Hq"], DECODE_1B["Hk"], DECODE_1B["D"]
+        L, B, H = len(self.layers), self.qkv.shape[1], HIDDEN_1B
+        N = (Hq + 2 * Hk) * D
+        g = torch.Generator(device=device)
+        g.manual_seed(31 + rank)
+        self.x = torch.randn(L, B, H, generator=g, device=device).half()
+        self.w = (torch.randn(L, H, N, generator=g, device=device) / math.sqrt(H)).half()
+        self.b = torch.randn(L, N, generator=g, device=device) * 0.1
+        self.lib = pkg.lib()
+        self.bytes_per_step += L * (H * N * 2 + B * H * 2)
+        self.bytes_per_launch = self.bytes_per_step / L
+        self.launches_per_step = 2 * L
+        self.kernel = "proj_tc_kernel<64> (QKV + QK-norm/RoPE/append epilogue) + decode_fast_kernel<64,half>"
+        self.config = dict(self.config, parallelism=f"batch-sharded x{world}",
+                           projection=f"x [{B}, {H}] @ W [{H}, {N}] fp16 + bias per layer")
+
+    def step(self, record=None):
+        import ctypes
+
+        s = ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
+        for i, layer in enumerate(self.layers):
+            rc = self.lib.tla_qkv_decode(layer.handle, ctypes.c_void_p(self.x[i].data_ptr()),
+                                         ctypes.c_void_p(self.w[i].data_ptr()), ctypes.c_void_p(self.b[i].data_ptr()),
+                                         HIDDEN_1B, ctypes.c_void_p(self.pos.data_ptr()), None,
+                                         ctypes.c_void_p(self.outs[i].data_ptr()), self.x.shape[1], s)
+            if rc:
+                raise RuntimeError(f"tla_qkv_decode: {rc}")
+
+    def parity(self, world, rank):
+        from oracle import oracle
+
+        t = self.torch
+        layer = self.layers[0]
+        Hq, Hk, D = layer.headCount, layer.kvHeadCount, layer.headDim
+        G, n = Hq // Hk, 4
+        pos = self.pos.cpu().numpy()
+        kc, vc = cache_tensors(t, layer)
+        T = int(pos[:n].max()) + 1
+        k_host = kc[:n, 0, :T].float().cpu().numpy().copy()
+        v_host = vc[:n, 0, :T].float().cpu().numpy().copy()
+        self.step()
+        out = self.outs[0, :n].float().cpu().numpy()
+        cols = np.r_[0:G * D, Hq * D:(Hq + 1) * D, (Hq + Hk) * D:(Hq + Hk + 1) * D]
+        x = self.x[0, :n].float().cpu().numpy()
+        w = self.w[0].float().cpu().numpy()[:, cols]
+        b = self.b[0].float().cpu().numpy()[cols]
+        qkv = oracle.linear(x, w, b, threads=oracle.cpu_count())
+        exp = oracle.decode_batch(qkv, pos[:n], k_host, v_host, threads=oracle.cpu_count(), head_count=G,
+                                  kv_head_count=1, head_dim=D, rope_theta=DECODE_1B["theta"])
+        err, ok = close_enough(out[:, :G * D], exp)
+        return {"max_abs_err": err, "ok": ok,
+                "checked": f"rank 0, layer 0: {n} sequences x query heads 0..{G - 1}: oracle linear + attention"}
+
+
+def run_qkv_prefill(pkg, torch, device, rank, world, args, tc):
+    """Config 3 from the hidden states (Qwen2-0.5B shapes, hidden 896): the fused
+    projection (tcgen05, QK-norm / RoPE / append epilogue) then the causal
+    tensor-core attention; the FLOPs counted are the projection's plus the
+    causal attention's."""
+    import ctypes
+
+    from three_llm_b200 import sharding
+
+    w_ = PREFILL_05B
+    B, S, Hq, Hk, D, H = w_["B"], w_["S"], w_["Hq"], w_["Hk"], w_["D"], HIDDEN_05B
+    sh = sharding.batch_head_shard(B, Hq, Hk, world, rank)
+    g = torch.Generator(device=device)
+    g.manual_seed(98)
+    N = (Hq + 2 * Hk) * D
+    x_full = torch.randn(B, S, H, generator=g, device=device).half()
+    w_full = (torch.randn(H, N, generator=g, device=device) / math.sqrt(H)).half()
+    b_full = torch.randn(N, generator=g, device=device) * 0.1
+    heads = list(range(sh.q_begin, sh.q_begin + sh.q_count)) + \
+        [Hq + k for k in range(sh.kv_begin, sh.kv_begin + sh.kv_count)] + \
+        [Hq + Hk + k for k in range(sh.kv_begin, sh.kv_begin + sh.kv_count)]
+    cols = torch.cat([torch.arange(h * D, (h + 1) * D, device=device) for h in heads])
+    x = x_full[sh.seq_begin:sh.seq_begin + sh.seq_count].contiguous()
+    w = w_full[:, cols].contiguous()
+    b = b_full[cols].contiguous()
+    layer = pkg.CUDAAttention(None, sh.q_count * D, sh.q_count, w_["T"],
+                              {"headDim": D, "kvHeadCount": sh.kv_count, "ropeTheta": w_["theta"],
+                               "maxBatch": sh.seq_count, "dtype": torch.float16})
+    start = torch.zeros(sh.seq_count, dtype=torch.int32, device=device)
+    out = torch.empty(sh.seq_count, S, sh.q_count * D, dtype=torch.float16, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    lib = pkg.lib()
+
+    def call():
+        rc = lib.tla_qkv_prefill(layer.handle, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                                 ctypes.c_void_p(b.data_ptr()), H, ctypes.c_void_p(start.data_ptr()), None, S,
+                                 ctypes.c_void_p(out.data_ptr()), sh.seq_count,
+                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        if rc:
+            raise RuntimeError(f"tla_qkv_prefill: {rc}")
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    est = timed_blocks(torch, call, args.steps, 1, world, per_call=flush.zero_)[0]
+    repeats = agree_repeats(torch, est, 0.05, world, lo=5, hi=200)
+    st = stats(timed_blocks(torch, call, args.steps, repeats, world, per_call=flush.zero_), args.steps)
+    if layer.context.error() != 0:
+        raise RuntimeError("device reported an error")
+    flops = prefill_causal_flops(D, S, B, Hq) + 2 * B * S * H * N
+    ms = st["median"]
+    rec = {"workload": "config 3 from hidden states: x [4, 2048, 896] @ W_qkv [896, 1152] + bias, QK-norm-free "
+                       "RoPE theta 1e6 + append in the GEMM epilogue, then causal attention; L2 flushed per call",
+           "parallelism": f"(sequence, kv-head group) units x{world}",
+           "tflops": round(flops / (ms * 1e-3) / 1e12, 2), "ms": round(ms, 5), "ms_p10": round(st["p10"], 5),
+           "ms_p90": round(st["p90"], 5), "gflop": round(flops / 1e9, 3),
+           "frac": round(flops / (ms * 1e-3) / 1e12 / world / tc, 4),
+           "kernels": "proj_tc_kernel<64> (QKV + RoPE/append epilogue) + prefill_tc_kernel<64,half>",
+           "gpu_launches": int(2 * st["blocks"] * args.steps)}
+    if rank == 0:  # first 256 positions of the rank's first sequence, first kv head's query group
+        from oracle import oracle
+
+        n, G = 256, sh.q_count // sh.kv_count
+        sub_heads = list(range(G)) + [sh.q_count, sh.q_count + sh.kv_count]
+        sc = torch.cat([torch.arange(h * D, (h + 1) * D, device=device) for h in sub_heads])
+        qkv = oracle.linear(x[0, :n].float().cpu().numpy(), w[:, sc].float().cpu().numpy(),
+                            b[sc].float().cpu().numpy(), threads=oracle.cpu_count())[None]
+        kc = np.zeros((1, n, D), np.float32)
+        vc = np.zeros_like(kc)
+        exp = oracle.prefill(qkv, [0], kc, vc, threads=oracle.cpu_count(), head_count=G, kv_head_count=1, head_dim=D,
+                             rope_theta=w_["theta"])
+        err, ok = close_enough(out[0, :n, :G * D].float().cpu().numpy(), exp[0])
+        rec["parity"] = {"max_abs_err": err, "ok": ok, "checked": f"rank 0: positions 0..{n - 1}, query heads of its "
+                                                                  "first kv head: oracle linear + replay"}
+    layer.close()
+    return rec
+
+
+def run_out_proj(pkg, torch, device, rank, world, args, hbm):
+    """The attention output projection + residual of config 4 (8B shapes: 32
+    query heads x d128 = 4096 inputs, hidden 4096), batch 64, 32 layers per
+    step. One GPU: tla_out_proj. N GPUs: the query heads are sharded, each rank
+    multiplies its 4096/N input columns by its rows of W and
+    tla_out_proj_allreduce sums the partials over NVLink (GEMM epilogue stores
+    into the owner's buffer, then one finishing kernel); beside it the same
+    partials summed by an NCCL all-reduce."""
+    from three_llm_b200 import sharding
+
+    rows, fin, H, L = 64, 32 * 128, HIDDEN_8B, 32
+    per = fin // world
+    g = torch.Generator(device=device)
+    g.manual_seed(61)  # the full problem on every rank
+    attn = torch.randn(L, rows, fin, generator=g, device=device).half()
+    w = (torch.randn(L, fin, H, generator=g, device=device) / math.sqrt(fin)).half()
+    bias = torch.randn(L, H, generator=g, device=device) * 0.1
+    res = torch.randn(L, rows, H, generator=g, device=device).half()
+    a_r = attn[:, :, rank * per:(rank + 1) * per].contiguous()
+    w_r = w[:, rank * per:(rank + 1) * per].contiguous()
+    del attn, w
+    y = torch.empty(L, rows, H, dtype=torch.float16, device=device)
+    ctx = pkg.Context.default(device.index or 0)
+    op = sharding.HeadShardedOutProj(rows, H, rank, world, device, context=ctx) if world > 1 else None
+    import ctypes
+
+    lib = pkg.lib()
+
+    def step():
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for i in range(L):
+            if op is not None:
+                op(a_r[i], w_r[i], bias[i], res[i], out=y[i])
+            else:
+                rc = lib.tla_out_proj(ctx.handle, ctypes.c_void_p(a_r[i].data_ptr()),
+                                      ctypes.c_void_p(w_r[i].data_ptr()), ctypes.c_void_p(bias[i].data_ptr()),
+                                      ctypes.c_void_p(res[i].data_ptr()), ctypes.c_void_p(y[i].data_ptr()), rows,
+                                      per, H, 0, s)
+                if rc:
+                    raise RuntimeError(f"tla_out_proj: {rc}")
+
+    def measure(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()  # the 32-layer step replayed as one graph
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph):
+            fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        est = timed_blocks(torch, graph.replay, args.steps, 1, world)[0]
+        out = stats(timed_blocks(torch, graph.replay, args.steps, agree_repeats(torch, est, 0.2, world), world),
+                    args.steps)
+        del graph  # may hold NCCL work: released before the process group goes away
+        torch.cuda.synchronize()
+        return out
+
+    st = measure(step)
+    if ctx.error() != 0:
+        raise RuntimeError("device reported an error")
+    ms = st["median"]
+    wbytes = L * per * H * 2 * world
+    rec = {"workload": "output projection + residual, 8B shapes: attn [64, 4096] @ W_o [4096, 4096] + bias + "
+                       "residual, 32 layers per step",
+           "parallelism": (f"query heads x{world}: partial GEMM per rank, NVLink reduce-scatter from the GEMM "
+                           "epilogue + all-gather kernel" if world > 1 else "one GPU"),
+           "ms_per_step": round(ms, 5), "ms_p10": round(st["p10"], 5), "ms_p90": round(st["p90"], 5),
+           "us_per_layer": round(ms * 1e3 / L, 2), "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1),
+           "frac": round(wbytes / world / (ms * 1e-3) / 1e9 / hbm, 4),
+           "gpu_launches": int(st["blocks"] * args.steps * L * (2 if world > 1 else 1))}
+    if world > 1:  # the same partial products summed by NCCL, for comparison
+        part = torch.empty(L, rows, H, dtype=torch.float32, device=device)
+
+        def nccl_step():
+            s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for i in range(L):
+                lib.tla_out_proj(ctx.handle, ctypes.c_void_p(a_r[i].data_ptr()), ctypes.c_void_p(w_r[i].data_ptr()),
+                                 None, None, ctypes.c_void_p(part[i].data_ptr()), rows, per, H, 4, s)
+                torch.distributed.all_reduce(part[i])
+                y[i].copy_(part[i] + bias[i] + res[i])
+
+        rec["nccl_allreduce_ms_per_step"] = round(measure(nccl_step)["median"], 5)
+    step()
+    torch.cuda.synchronize()
+    if rank == 0:  # 8 rows of layer 0 against the oracle's full (unsharded) product
+        from oracle import oracle
+
+        g2 = torch.Generator(device=device)
+        g2.manual_seed(61)
+        attn0 = torch.randn(L, rows, fin, generator=g2, device=device).half()[0, :8].float().cpu().numpy()
+        w0 = (torch.randn(L, fin, H, generator=g2, device=device) / math.sqrt(fin)).half()[0].float().cpu().numpy()
+        exp = oracle.linear(attn0, w0, bias[0].cpu().numpy(), threads=oracle.cpu_count()) + \
+            res[0, :8].float().cpu().numpy()
+        err, ok = close_enough(y[0, :8].float().cpu().numpy(), exp)
+        rec["parity"] = {"max_abs_err": err, "ok": ok, "checked": "rank 0, layer 0, rows 0..7 vs oracle linear + "
+                                                                  "residual over all 4096 inputs"}
+    if op is not None:
+        op.close()
+    return rec
+
+
 # ---------------------------------------------------------------- CPU legs (oracle, torch eager)
 def cpu_decode_sample(threads, workload="decode_1b", batch=4, heads=None, min_seconds=0.0):
     """Time the oracle's attention loops (the reference's causalAttention restated) on a
@@ -1003,11 +1255,16 @@ def main():
             line["long_ctx_seq"] = dict(line["long_ctx_heads"], note="one GPU holds every token block: the plain "
                                                                      "decode of long_ctx_heads")
         line["prefill"] = guarded(run_prefill, pkg, torch, device, rank, world, args, tc, src)
+        line["qkv_decode_1b"] = guarded(sub_decode, "qkv_decode_1b", QkvDecode1B, pkg, torch, device, rank, world,
+                                        args, hbm)
+        line["prefill_qkv"] = guarded(run_qkv_prefill, pkg, torch, device, rank, world, args, tc)
+        line["out_proj"] = guarded(run_out_proj, pkg, torch, device, rank, world, args, hbm)
         for key in ("ragged_8b", "long_ctx_heads", "long_ctx_seq"):
             line[key].setdefault("workload", WORKLOAD_LABELS["long_ctx" if key.startswith("long") else key])
     if rank == 0:
         checks = [line.get("parity")] + [line.get(k, {}).get("parity") for k in
-                                         ("ragged_8b", "long_ctx_heads", "long_ctx_seq", "prefill")]
+                                         ("ragged_8b", "long_ctx_heads", "long_ctx_seq", "prefill", "qkv_decode_1b",
+                                          "prefill_qkv", "out_proj")]
         checks = [c for c in checks if c]
         line["parity_ok"] = bool(checks) and all(c["ok"] for c in checks)
         line["parity_max_err"] = max(c["max_abs_err"] for c in checks) if checks else None

@@ -246,6 +246,20 @@ int tla_exchange_buffer(tla_exchange* exchange, void** buffer_out);
 int tla_exchange_connect_buffers(tla_exchange* exchange, void* const* buffers /* [ranks] */);
 int tla_exchange_destroy(tla_exchange* exchange);
 
+/* tla_out_proj across the GPUs of a head-sharded layer (no counterpart in the reference, which runs on
+ * one device). attn [rows][in_features] holds this rank's query heads' attention output and weight
+ * ([in_features][hidden] fp16) the matching rows of W. The product runs on the tensor cores and its
+ * epilogue stores each partial tile over NVLink straight into the exchange buffer of the rank that owns
+ * those hidden columns (hidden / ranks each: a reduce-scatter fused into the GEMM); then one kernel sums
+ * the owned block over every rank, adds bias and residual and sends the block to every rank, so each rank
+ * ends with y = residual + sum over ranks of attn_r W_r + bias, [rows][hidden] (fp16, or float32 with
+ * TLA_FLAG_IO_FP32). The exchange's slot_bytes must hold 2 * rows * hidden / ranks floats and hidden must
+ * be a multiple of 64 * ranks. Every rank calls it with the same shapes, the same number of times; the
+ * waits are bounded (TLA_ERR_TIMEOUT through tla_get_error). */
+int tla_out_proj_allreduce(tla_exchange* exchange, const void* attn, const void* weight, const float* bias,
+                           const void* residual, void* y, int32_t rows, int32_t in_features, int32_t hidden,
+                           uint32_t io_flags, void* stream);
+
 /* tla_decode_partial fused with the exchange: this rank's split-KV decode
  * over its token block, then one kernel that merges each query row's segments,
  * exchanges the row's triple with every rank of `exchange` and writes the

@@ -175,8 +175,28 @@ def _rank_main(rank, world, port, result_path):
             out = gout.float().cpu().numpy()
             errs.append(float(np.max(np.abs(out - exp[i]) - (2e-3 + 1e-2 * np.abs(exp[i])))))
         torch.cuda.synchronize()
-        errs.append(float(layer.layer.context.error()))
         del graph
+        # the output projection of head-sharded attention (query heads split
+        # over the ranks), summed over NVLink by tla_out_proj_allreduce
+        rows, fin, hidden = 16, Hq * D, 1024
+        attn = rng.standard_normal((rows, fin)).astype(np.float16).astype(np.float32)
+        w = (rng.standard_normal((fin, hidden)) / np.sqrt(fin)).astype(np.float16).astype(np.float32)
+        bias = rng.standard_normal(hidden).astype(np.float32)
+        res = rng.standard_normal((rows, hidden)).astype(np.float16).astype(np.float32)
+        per = fin // world
+        op = sharding.HeadShardedOutProj(rows, hidden, rank, world, dev, context=layer.layer.context)
+        dist.barrier()
+        for _ in range(2):
+            y = op(torch.from_numpy(attn[:, rank * per:(rank + 1) * per]).to(dev, torch.float16).contiguous(),
+                   torch.from_numpy(w[rank * per:(rank + 1) * per]).to(dev, torch.float16).contiguous(),
+                   torch.from_numpy(bias).to(dev), torch.from_numpy(res).to(dev, torch.float16))
+            exp_y = oracle.linear(attn, w, bias, threads=4) + res
+            got = y.float().cpu().numpy()
+            errs.append(float(np.max(np.abs(got - exp_y) - (2e-3 + 1e-2 * np.abs(exp_y)))))
+        torch.cuda.synchronize()
+        dist.barrier()
+        op.close()
+        errs.append(float(layer.layer.context.error()))
         layer.close()
         dist.barrier()
     finally:

@@ -151,3 +151,30 @@ def test_out_proj_residual_vs_oracle(pkg, cuda, rows, fin, hidden, f32):
     assert ctx.error() == 0
     exp = oracle.linear(attn, w, bias, threads=THREADS) + res
     assert_close(y.float().cpu().numpy(), exp, what="output projection + residual")
+
+
+def test_out_proj_allreduce_one_rank_vs_oracle(pkg, cuda):
+    """The head-sharded path with a single rank: the GEMM's partial tiles go
+    through the exchange buffer (epoch words) and the finishing kernel adds
+    bias and residual; three calls in a row cover both buffer parities."""
+    from three_llm_b200 import sharding
+
+    rng = np.random.default_rng(17)
+    rows, fin, hidden = 64, 1024, 2048
+    w, bias = weights(rng, fin, hidden)
+    wd, bd = torch.from_numpy(w).to(cuda, torch.float16), torch.from_numpy(bias).to(cuda)
+    op = sharding.HeadShardedOutProj(rows, hidden, 0, 1, cuda.index or 0, group=False)
+    try:
+        op.exchange.connect_buffers([op.exchange.buffer()])
+        for call in range(3):
+            attn = f16(rng.standard_normal((rows, fin)))
+            res = f16(rng.standard_normal((rows, hidden)))
+            y = op(torch.from_numpy(attn).to(cuda, torch.float16), wd, bd,
+                   torch.from_numpy(res).to(cuda, torch.float16))
+            torch.cuda.synchronize()
+            assert op.exchange.context.error() == 0
+            exp = oracle.linear(attn, w, bias, threads=THREADS) + res
+            assert_close(y.float().cpu().numpy(), exp, what=f"all-reduce output projection, call {call}")
+    finally:
+        op.close()
+

@@ -32,7 +32,7 @@ EXPORTS = [
     "tla_decode_partial", "tla_combine_lse", "tla_cache_reset", "tla_cache_read", "tla_cache_write",
     "tla_decode_noalloc", "tla_exchange_create", "tla_exchange_connect", "tla_exchange_combine",
     "tla_exchange_buffer", "tla_exchange_connect_buffers", "tla_exchange_destroy", "tla_decode_exchange",
-    "tla_query", "tla_scores", "tla_qkv_decode", "tla_qkv_prefill", "tla_out_proj",
+    "tla_query", "tla_scores", "tla_qkv_decode", "tla_qkv_prefill", "tla_out_proj", "tla_out_proj_allreduce",
 ]
 
 
@@ -117,6 +117,7 @@ def lib():
         L.tla_qkv_decode.argtypes = [P, P, P, P, i32, P, P, P, i32, P]
         L.tla_qkv_prefill.argtypes = [P, P, P, P, i32, P, P, i32, P, i32, P]
         L.tla_out_proj.argtypes = [P, P, P, P, P, P, i32, i32, i32, u32, P]
+        L.tla_out_proj_allreduce.argtypes = [P, P, P, P, P, P, i32, i32, i32, u32, P]
         L.tla_decode_partial.argtypes = [P, P, P, i32, i32, i32, P, i32, P]
         L.tla_combine_lse.argtypes = [P, i32, i32, i32, i32, P, P, u32, P]
         L.tla_cache_reset.argtypes = [P, P]

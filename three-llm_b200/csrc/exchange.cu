@@ -183,6 +183,28 @@ int tla_exchange_combine(tla_exchange* ex, const float* partial, int32_t batch, 
   return e == cudaSuccess ? TLA_OK : TLA_ERR_CUDA;
 }
 
+int tla_out_proj_allreduce(tla_exchange* ex, const void* attn, const void* weight, const float* bias,
+                           const void* residual, void* y, int32_t rows, int32_t in_features, int32_t hidden,
+                           uint32_t io_flags, void* stream) {
+  if (!ex || !ex->connected || !attn || !weight || !y || rows < 0 || in_features <= 0 || in_features % 64 != 0 ||
+      hidden <= 0 || hidden % (64 * ex->ranks) != 0)
+    return TLA_ERR_INVALID_ARG;
+  if (2 * static_cast<size_t>(rows) * (hidden / ex->ranks) * sizeof(float) > ex->slot_bytes)
+    return TLA_ERR_INVALID_ARG;
+  if (ex->ctx->encode_tiled == nullptr) return TLA_ERR_UNSUPPORTED;
+  if (rows == 0) return TLA_OK;
+  tla::ExchangeDev x;
+  tla::exchange_device_view(ex, &x);
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(ex->ctx->device);
+  const cudaError_t e =
+      tla::launch_out_proj_allreduce(ex->ctx, x, attn, weight, bias, residual, (io_flags & TLA_FLAG_IO_FP32) != 0, y,
+                                     rows, in_features, hidden, static_cast<cudaStream_t>(stream));
+  if (prev >= 0) cudaSetDevice(prev);
+  return e == cudaSuccess ? TLA_OK : TLA_ERR_CUDA;
+}
+
 int tla_exchange_destroy(tla_exchange* ex) {
   if (!ex) return TLA_OK;
   int prev = -1;

@@ -22,6 +22,7 @@
 // lane. Every mbarrier wait is bounded (TLA_ERR_TIMEOUT).
 #include <math.h>
 
+#include "exchange.cuh"
 #include "tcgen05.cuh"
 #include "tla_device.cuh"
 #include "tla_internal.h"
@@ -33,7 +34,7 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kXStage = 128 * 128;  // x: 128 rows x 64 fp16 (one 128-byte row each)
 constexpr int kWBox = 64 * 128;     // W: 64 rows of the reduction dim x 64 fp16 columns
-enum : int { kQkvDecode = 0, kQkvPrefill = 1, kOutProj = 2 };
+enum : int { kQkvDecode = 0, kQkvPrefill = 1, kOutProj = 2, kOutPush = 3 };
 
 struct ProjParams {
   CUtensorMap tm_x;  // [rows][K] fp16, box {64, 128}
@@ -52,13 +53,18 @@ struct ProjParams {
   const void* residual;  // [rows][N] or null
   void* y;               // [rows][N]
   int y_f32, res_f32;    // float32 (else fp16) output / residual
+  // head-sharded output projection: the partial tile goes over NVLink to the
+  // rank that owns its columns (cols = hidden / ranks each), as {value, epoch}
+  // words in that rank's exchange buffer, slot [this rank], first half
+  ExchangeDev x;
+  int cols;
 };
 
 __host__ __device__ inline int stage_bytes(int NT) { return kXStage + (NT / 64) * kWBox; }
 
 template <int D>
 __host__ __device__ inline int epilogue_bytes(int mode) {
-  return mode == kOutProj ? 0 : 2 * kThreads * (D + 1) * 4;  // each row's head values and its cos / sin
+  return mode >= kOutProj ? 0 : 2 * kThreads * (D + 1) * 4;  // each row's head values and its cos / sin
 }
 
 template <int D>
@@ -96,6 +102,8 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   griddep_wait();  // x, positions and the residual may come from the previous kernel
+  __shared__ int epoch_s;
+  const unsigned epoch = p.mode == kOutPush ? xch_epoch(p.x, &epoch_s) : 0u;  // (block-uniform branch)
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     if (*abort_flag) return;
     if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
@@ -145,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
   const int r = tid, row = m0 + r;
   const bool valid = row < p.rows;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  if (p.mode != kOutProj) {
+  if (p.mode == kQkvDecode || p.mode == kQkvPrefill) {
     // ---------------------------------------------------------------- QKV epilogue
     const LayerArgs& a = p.a;
     int b = 0, t = 0, pos = -1;
@@ -229,6 +237,21 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
         }
         *reinterpret_cast<uint4*>(dst + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
+    }
+  } else if (p.mode == kOutPush) {
+    // ---------------------------------------------------------------- partial tile -> its owner over NVLink
+    const int owner = n0 / p.cols;  // NT divides cols: the tile lies in one owner's block
+    uint8_t* dst = p.x.peers[owner] + static_cast<size_t>(epoch & 1u) * p.x.region_bytes;
+    const size_t word0 = static_cast<size_t>(p.x.rank) * p.x.slot_words + static_cast<size_t>(row) * p.cols +
+                         (n0 - owner * p.cols);
+    for (int c = 0; c < p.NT / 32; ++c) {
+      float v[32];
+      tmem_ld32(lane_base + 32 * c, v);
+      if (!valid) continue;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        xch_st_v4(dst + (word0 + 32 * c + 2 * i) * 8,
+                  make_uint4(__float_as_uint(v[2 * i]), epoch, __float_as_uint(v[2 * i + 1]), epoch));
     }
   } else {
     // ---------------------------------------------------------------- output projection epilogue
@@ -328,7 +351,133 @@ cudaError_t launch_proj_t(const tla_ctx* ctx, ProjParams& p, cudaStream_t stream
   return launch_pdl(proj_tc_kernel<D>, static_cast<unsigned>(p.m_tiles * n_tiles), kThreads, smem, stream, p);
 }
 
+// Second half of the head-sharded output projection, one 128-thread CTA per SM
+// at most (every CTA a peer waits for is resident): each thread takes pairs of
+// this rank's column block, waits (bounded) for every rank's partial words of
+// the pair, sums them in rank order, adds bias and residual, keeps the result
+// and stores it into slot [this rank], second half, of every rank's buffer;
+// then it collects the other ranks' finished blocks. Every CTA finishes its
+// own block's pairs before it waits on another rank's.
+template <typename OUT>
+__global__ void __launch_bounds__(128) out_allreduce_kernel(ExchangeDev x, int rows, int hidden, int cols,
+                                                            const float* __restrict__ bias, const void* residual,
+                                                            int res_f32, OUT* __restrict__ y, int* error) {
+  __shared__ int epoch_s;
+  griddep_wait();  // the partial tiles of this rank's GEMM are out
+  const unsigned epoch = xch_epoch(x, &epoch_s);
+  const uint8_t* mine = x.peers[x.rank] + static_cast<size_t>(epoch & 1u) * x.region_bytes;
+  volatile int* abort_p = reinterpret_cast<volatile int*>(x.peers[x.rank] + 2 * x.region_bytes + 256);
+  const size_t half_words = static_cast<size_t>(rows) * cols;  // second half of a slot
+  const int pairs = static_cast<int>(half_words / 2);
+  const int stride = static_cast<int>(gridDim.x * blockDim.x);
+  auto wait_words = [&](uint4 (&w)[kXchMaxRanks], size_t word, int only) {
+    // only < 0: every rank's slot; else just slot `only`
+    auto load = [&](int r) { return xch_ld_v4(mine + (static_cast<size_t>(r) * x.slot_words + word) * 8); };
+#pragma unroll
+    for (int r = 0; r < kXchMaxRanks; ++r)
+      if (r < x.ranks && (only < 0 || r == only)) w[r] = load(r);
+    unsigned long long t0 = 0;
+    for (;;) {
+      bool done = true;
+#pragma unroll
+      for (int r = 0; r < kXchMaxRanks; ++r)
+        if (r < x.ranks && (only < 0 || r == only) && (w[r].y != epoch || w[r].w != epoch)) {
+          done = false;
+          w[r] = load(r);
+        }
+      if (done || *abort_p == static_cast<int>(epoch)) return;
+      const unsigned long long now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        report_error(error, TLA_ERR_TIMEOUT);
+        *abort_p = static_cast<int>(epoch);
+        return;
+      }
+    }
+  };
+  auto store = [&](int row, int col, float v0, float v1) {
+    const size_t o = static_cast<size_t>(row) * hidden + col;
+    if constexpr (sizeof(OUT) == 4)
+      *reinterpret_cast<float2*>(y + o) = make_float2(v0, v1);
+    else
+      *reinterpret_cast<uint32_t*>(y + o) = pack_half2(v0, v1);
+  };
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
+    const int row = (2 * i) / cols, lc = 2 * i - row * cols, col = x.rank * cols + lc;
+    uint4 w[kXchMaxRanks];
+    wait_words(w, static_cast<size_t>(2 * i), -1);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int r = 0; r < kXchMaxRanks; ++r)
+      if (r < x.ranks) {
+        s0 += __uint_as_float(w[r].x);
+        s1 += __uint_as_float(w[r].z);
+      }
+    if (bias) {
+      s0 += __ldg(bias + col);
+      s1 += __ldg(bias + col + 1);
+    }
+    if (residual) {
+      const size_t o = static_cast<size_t>(row) * hidden + col;
+      if (res_f32) {
+        const float2 q = *reinterpret_cast<const float2*>(static_cast<const float*>(residual) + o);
+        s0 += q.x;
+        s1 += q.y;
+      } else {
+        const __half2 q = *reinterpret_cast<const __half2*>(static_cast<const __half*>(residual) + o);
+        s0 += __low2float(q);
+        s1 += __high2float(q);
+      }
+    }
+    store(row, col, s0, s1);
+    const uint4 out = make_uint4(__float_as_uint(s0), epoch, __float_as_uint(s1), epoch);
+    const size_t word = static_cast<size_t>(x.rank) * x.slot_words + half_words + 2 * i;
+    for (int q = 0; q < x.ranks; ++q)
+      if (q != x.rank) xch_st_v4(x.peers[q] + static_cast<size_t>(epoch & 1u) * x.region_bytes + word * 8, out);
+  }
+  for (int q = 0; q < x.ranks; ++q) {
+    if (q == x.rank) continue;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
+      const int row = (2 * i) / cols, lc = 2 * i - row * cols;
+      uint4 w[kXchMaxRanks];
+      wait_words(w, half_words + 2 * i, q);
+      store(row, q * cols + lc, __uint_as_float(w[q].x), __uint_as_float(w[q].z));
+    }
+  }
+  xch_finish(x, epoch);
+}
+
 }  // namespace
+
+cudaError_t launch_out_proj_allreduce(const tla_ctx* ctx, const ExchangeDev& x, const void* attn,
+                                      const void* weight, const float* bias, const void* residual, bool f32, void* y,
+                                      int rows, int in_features, int hidden, cudaStream_t stream) {
+  ProjParams p{};
+  if (make_map_2d(ctx, attn, in_features, rows, 128, &p.tm_x) != CUDA_SUCCESS ||
+      make_map_2d(ctx, weight, hidden, in_features, 64, &p.tm_w) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  p.rows = rows;
+  p.K = in_features;
+  p.N = hidden;
+  p.cols = hidden / x.ranks;
+  p.m_tiles = (rows + 127) / 128;
+  p.NT = choose_nt(p.cols, 64, p.m_tiles * x.ranks, ctx->sm_count);  // NT divides an owner's block
+  if (p.NT == 0) return cudaErrorInvalidValue;
+  p.mode = kOutPush;
+  p.error = ctx->d_error;
+  p.x = x;
+  cudaError_t e = launch_proj_t<64>(ctx, p, stream);
+  if (e != cudaSuccess) return e;
+  const int pairs = rows * p.cols / 2;
+  int grid = (pairs + 127) / 128;
+  if (grid > ctx->sm_count) grid = ctx->sm_count;
+  if (f32)
+    return launch_pdl(out_allreduce_kernel<float>, static_cast<unsigned>(grid), 128, 0, stream, x, rows, hidden,
+                      p.cols, bias, residual, 1, static_cast<float*>(y), ctx->d_error);
+  return launch_pdl(out_allreduce_kernel<__half>, static_cast<unsigned>(grid), 128, 0, stream, x, rows, hidden,
+                    p.cols, bias, residual, 0, static_cast<__half*>(y), ctx->d_error);
+}
 
 cudaError_t launch_qkv_proj(const tla_layer* L, const void* x, const void* weight, const float* bias, int hidden,
                             const int32_t* pos, int rows, int seq_len, bool prefill, __half* qout,

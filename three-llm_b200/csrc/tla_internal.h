@@ -155,6 +155,12 @@ cudaError_t launch_decode_fast_qrot(const tla_layer* L, const __half* qrot, cons
 cudaError_t launch_qkv_proj(const tla_layer* L, const void* x, const void* weight, const float* bias, int hidden,
                             const int32_t* pos, int rows, int seq_len, bool prefill, __half* qout,
                             cudaStream_t stream);
+// Head-sharded output projection: this rank's partial product tiles are stored
+// over NVLink into the exchange buffer of the rank owning their columns, then
+// one kernel sums the owned block, adds bias + residual and all-gathers.
+cudaError_t launch_out_proj_allreduce(const tla_ctx* ctx, const ExchangeDev& x, const void* attn,
+                                      const void* weight, const float* bias, const void* residual, bool f32, void* y,
+                                      int rows, int in_features, int hidden, cudaStream_t stream);
 cudaError_t launch_out_proj(const tla_ctx* ctx, const void* attn, const void* weight, const float* bias,
                             const void* residual, bool residual_f32, void* y, bool y_f32, int rows, int in_features,
                             int hidden, cudaStream_t stream);

@@ -213,3 +213,39 @@ class SequenceShardedDecode:
             self.exchange.close()
         self.exchange = None
         self.layer.close()
+
+
+class HeadShardedOutProj:
+    """Output projection + residual after head-sharded attention
+    (DecoderTSLRunner.ts:299-309: attnProj, then TSLAdd), across the ranks:
+    tla_out_proj_allreduce multiplies this rank's attention columns by its rows
+    of W on the tensor cores, the GEMM epilogue stores each partial tile over
+    NVLink into the exchange buffer of the rank owning those hidden columns,
+    and one kernel sums each owned block, adds bias + residual and sends it to
+    every rank. Every rank ends with the full y [rows, hidden]."""
+
+    def __init__(self, rows, hidden, rank, world, device=None, group=None, context=None, exchange=None):
+        if hidden % (64 * world):
+            raise ValueError("hidden must be a multiple of 64 * world")
+        self.rows, self.hidden = rows, hidden
+        slot = 2 * rows * (hidden // world) * 4
+        self.owns = exchange is None
+        self.exchange = exchange or PeerExchange(rank, world, slot, device, group, context)
+
+    def __call__(self, attn, weight, bias=None, residual=None, out=None, stream=None):
+        """attn [rows, in_r] fp16 (this rank's heads), weight [in_r, hidden] fp16 (its rows of W)."""
+        rows, fin = attn.shape
+        f32 = residual is not None and residual.dtype == torch.float32
+        if out is None:
+            out = torch.empty(rows, self.hidden, dtype=torch.float32 if f32 else torch.float16, device=attn.device)
+        check(lib().tla_out_proj_allreduce(self.exchange.handle, _ptr(attn), _ptr(weight), _ptr(bias),
+                                           _ptr(residual), _ptr(out), rows, fin, self.hidden,
+                                           _abi.FLAG_IO_FP32 if out.dtype == torch.float32 else 0, _stream(stream)),
+              "tla_out_proj_allreduce")
+        return out
+
+    def close(self):
+        if self.owns and self.exchange is not None:
+            self.exchange.close()
+        self.exchange = None
+
