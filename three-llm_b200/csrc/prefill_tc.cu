@@ -62,12 +62,16 @@ __device__ __forceinline__ float ex2_poly(float x) {
 __device__ unsigned long long g_prefill_trace[64][16];
 #define PTRACE(ev, n) \
   do { \
-    if (blockIdx.x == 0 && (n) < 64) g_prefill_trace[(n)][(ev)] = clock64(); \
+    if (blockIdx.x == 0 && pipe == 0 && (n) < 64) g_prefill_trace[(n)][(ev)] = clock64(); \
   } while (0)
 #else
 #define PTRACE(ev, n) \
   do { \
   } while (0)
+#endif
+
+#ifndef TLA_PREFILL_DUAL
+#define TLA_PREFILL_DUAL 0  // head_dim 64: two pipelines per CTA (measured slower; 0: one)
 #endif
 
 #ifndef TLA_PREFILL_POLY_EVERY
@@ -193,18 +197,27 @@ __device__ __forceinline__ void load_row32(const T* src, float (&v)[32]) {
 // same barrier: P V(g-1) needs P(g-1), which the softmax releases only after
 // it has loaded S(g), also across items.
 // TMEM columns: S/P buffer j at 128 j (j < NS), O buffer i at 128 NS + D i (i < NO).
-constexpr int kThreads = 224;  // warps 0-3: softmax, 4: TMA, 5: P V issuer (and TMEM owner), 6: S issuer
-constexpr int kMmaWarp = 5, kTmaWarp = 4, kSWarp = 6;
+// Warp roles. One pipeline: warps 0-3 softmax, 4 TMA, 5 P V issuer (and TMEM
+// owner), 6 S issuer (224 threads). Two pipelines (DUAL, head_dim 64): each
+// CTA runs two independent copies of that pipeline over alternate work items,
+// each with one TMEM S buffer, so one pipeline's exponentials overlap the
+// other's MMAs and loads: warps 0-3 / 4-7 softmax of pipeline 0 / 1, 8-9 TMA,
+// 10-11 P V issuers (warp 10 owns TMEM), 12-13 S issuers, 14-15 idle (they
+// complete the fourth warpgroup for setmaxnreg), 512 threads.
+enum : int { kRoleSoftmax = 0, kRoleTma = 1, kRolePv = 2, kRoleS = 3, kRoleIdle = 4 };
 
-template <int D>
+template <int D, bool DUAL = false>
 struct PCfg {
+  static constexpr int kPipes = DUAL ? 2 : 1;
+  static constexpr int kThreads = DUAL ? 512 : 224;
+  static constexpr int kAllocWarp = DUAL ? 10 : 5;
   static constexpr int kBoxes = D / 64;
   static constexpr int kBox = 128 * 128;         // [128 rows][64 fp16]
   static constexpr int kTile = kBoxes * kBox;    // Q tile, or K (V) of one step
-  static constexpr int kNS = 3;                  // TMEM S buffers
+  static constexpr int kNS = DUAL ? 1 : 3;       // TMEM S buffers (per pipeline)
   static constexpr int kNO = D == 64 ? 2 : 1;    // TMEM O buffers (by item)
-  static constexpr int kNQ = D == 64 ? 2 : 1;    // Q tiles in shared memory (by item)
-  static constexpr int kST = D == 64 ? 4 : 3;    // K/V stages (K and V rings are filled independently)
+  static constexpr int kNQ = (D == 64 && !DUAL) ? 2 : 1;  // Q tiles in shared memory (by item)
+  static constexpr int kST = DUAL ? 2 : (D == 64 ? 4 : 3);  // K/V stages (K and V rings filled independently)
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + kNQ * kTile;
   static constexpr int kV = kK + kST * kTile;
@@ -213,12 +226,15 @@ struct PCfg {
   // the K/V stages take the room)
   static constexpr int kOut = kV + kST * kTile;
   static constexpr int kOutBytes = D == 64 ? 4 * 32 * D * 4 : 0;
-  static constexpr int kBar = kOut + kOutBytes;
-  // q_full, q_empty [2]; k_full, v_full, k_empty, v_empty [kST]; s_full, p_full [kNS]; o_done, o_free [2]
+  static constexpr int kPipeBytes = kOut + kOutBytes;  // one pipeline's shared memory (1024-aligned)
+  static constexpr int kBar = kPipes * kPipeBytes;
+  // per pipeline: q_full, q_empty [2]; k_full, v_full, k_empty, v_empty [kST];
+  // s_full, p_full [kNS]; o_done, o_free [2]
   static constexpr int kNumBars = 4 + 4 * kST + 2 * kNS + 4;
-  static constexpr int kSmem = kBar + kNumBars * 8 + 16 + 1024;
-  static constexpr uint32_t kO = 128 * kNS, kCols = 512;
-  static_assert(kO + kNO * D <= kCols, "TMEM columns");
+  static constexpr int kSmem = kBar + kPipes * kNumBars * 8 + 16 + 1024;
+  static constexpr uint32_t kO = 128 * kNS, kCols = 512, kPipeCols = kCols / kPipes;
+  static_assert(kO + kNO * D <= kPipeCols, "TMEM columns");
+  static_assert(kPipeBytes % 1024 == 0, "pipeline base alignment");
 };
 
 // A work item and its step range: item it (longest first) -> query tile m of
@@ -250,14 +266,25 @@ __device__ __forceinline__ int prefill_item_of(int k, int num_items) {
   return it < num_items ? it : -1;
 }
 
-template <int D, typename OUT>
-__global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
-  using C = PCfg<D>;
+template <int D, typename OUT, bool DUAL>
+__global__ void __launch_bounds__(PCfg<D, DUAL>::kThreads, 1)
+    prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
+  using C = PCfg<D, DUAL>;
   constexpr int kT = 128, NS = C::kNS;
   static_assert(NS <= 3, "the o_done parity argument needs S(g) to be issued after P V(g-3) or later");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int role, pipe = 0;
+  if constexpr (DUAL) {
+    role = warp < 8 ? kRoleSoftmax : (warp < 10 ? kRoleTma : (warp < 12 ? kRolePv : (warp < 14 ? kRoleS : kRoleIdle)));
+    pipe = warp < 8 ? warp >> 2 : (warp - 8) & 1;
+  } else {
+    role = warp < 4 ? kRoleSoftmax : (warp == 4 ? kRoleTma : (warp == 5 ? kRolePv : kRoleS));
+  }
+  uint8_t* const ps = smem + pipe * C::kPipeBytes;  // this pipeline's shared memory
+  uint64_t* const bars0 = reinterpret_cast<uint64_t*>(smem + C::kBar);
+  uint64_t* bars = bars0 + pipe * C::kNumBars;
   uint64_t* q_full = bars;  // [item % NQ]
   uint64_t* q_empty = bars + 2;
   uint64_t* k_full = bars + 4;
@@ -268,32 +295,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   uint64_t* p_full = s_full + NS;       // [g % NS]
   uint64_t* o_done = p_full + NS;       // [g & 1]
   uint64_t* o_free = o_done + 2;        // [item % NO]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars0 + C::kPipes * C::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int num_items = p.num_m * p.batch * p.Hq;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-      mbar_init(&o_done[i], 1);
-      mbar_init(&o_free[i], 128);
-    }
-    for (int i = 0; i < C::kST; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-      mbar_init(&v_empty[i], 1);
-    }
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+    for (int pp = 0; pp < C::kPipes; ++pp) {
+      uint64_t* b = bars0 + pp * C::kNumBars;
+      for (int i = 0; i < 4 + 4 * C::kST; ++i) mbar_init(&b[i], 1);  // q, k, v rings
+      for (int i = 0; i < NS; ++i) {
+        mbar_init(&b[4 + 4 * C::kST + i], 1);       // s_full
+        mbar_init(&b[4 + 4 * C::kST + NS + i], 128);  // p_full
+      }
+      mbar_init(&b[4 + 4 * C::kST + 2 * NS], 1);        // o_done [2]
+      mbar_init(&b[4 + 4 * C::kST + 2 * NS + 1], 1);
+      mbar_init(&b[4 + 4 * C::kST + 2 * NS + 2], 128);  // o_free [2]
+      mbar_init(&b[4 + 4 * C::kST + 2 * NS + 3], 128);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == C::kAllocWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(C::kCols)
                  : "memory");
@@ -302,14 +324,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *tmem_slot + static_cast<uint32_t>(pipe) * C::kPipeCols;  // this pipeline's columns
   griddep_wait();  // the RoPE/append kernel's queries and cache rows are complete
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     if (*abort_flag) return;
     if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
   };
 
-  if (warp == kTmaWarp) {
+  if (role != kRoleSoftmax) {
+  // Two pipelines: 512 threads x 128 registers at launch; the two control
+  // warpgroups (warps 8-15) give theirs down to 56 and the two softmax
+  // warpgroups take 200 (2 x 128 x 56 + 2 x 128 x 200 = 65536, the launch's
+  // total). setmaxnreg is issued once per warpgroup branch, by all four of its
+  // warps.
+  if constexpr (DUAL) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+  if (role == kRoleTma) {
     // ================================================================ TMA producer
     // lane 0: Q of each item, then its K tiles; lane 1: the V tiles. S runs
     // up to NS steps ahead of P V, so K must not queue behind V.
@@ -317,12 +346,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const CUtensorMap* map = lane == 0 ? &p.tm_k : &p.tm_v;
       uint64_t* full = lane == 0 ? k_full : v_full;
       uint64_t* empty = lane == 0 ? k_empty : v_empty;
-      uint8_t* ring = smem + (lane == 0 ? C::kK : C::kV);
+      uint8_t* ring = ps + (lane == 0 ? C::kK : C::kV);
       tma_prefetch(map);
       if (lane == 0) tma_prefetch(&p.tm_q);
       int g = 0;
       for (int k = 0;; ++k) {
-        const int it = prefill_item_of(k, num_items);
+        const int it = prefill_item_of(k * C::kPipes + pipe, num_items);
         if (it < 0) break;
         const PrefillItem w = prefill_item(p, it);
         const int z = w.b * p.Hk + w.h / p.G;
@@ -333,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             mbar_arrive_expect_tx(&q_full[qi], C::kTile);
 #pragma unroll
             for (int x = 0; x < C::kBoxes; ++x)
-              tma_load_3d(smem + C::kQ + qi * C::kTile + x * C::kBox, &p.tm_q, &q_full[qi], x * 64, w.row0,
+              tma_load_3d(ps + C::kQ + qi * C::kTile + x * C::kBox, &p.tm_q, &q_full[qi], x * 64, w.row0,
                           w.b * p.Hq + w.h);
           }
         }
@@ -351,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       for (int q = max(0, g - C::kST); q < g; ++q)  // no copies in flight at exit
         wait(&full[q % C::kST], (q / C::kST) & 1);
     }
-  } else if (warp == kMmaWarp || warp == kSWarp) {
+  } else if (role == kRolePv || role == kRoleS) {
     // ================================================================ MMA issuers
     // Two issuing threads, so that one's waits, commits and bookkeeping
     // overlap the other's MMAs: warp kSWarp issues every S(g) (S(g) for
@@ -367,12 +396,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       };
       // Descriptors are linear in the start address (bits 0-13 = addr >> 4, no
       // carry below 256 KB), so buffer, stage, box and k-step offsets are plain adds.
-      const uint64_t dq = sdesc(smem_u32(smem + C::kQ), 16, 1024);
-      const uint64_t dk = sdesc(smem_u32(smem + C::kK), 16, 1024);
-      const uint64_t dv = sdesc(smem_u32(smem + C::kV), C::kBox, 1024);
-      if (warp == kSWarp) {
+      const uint64_t dq = sdesc(smem_u32(ps + C::kQ), 16, 1024);
+      const uint64_t dk = sdesc(smem_u32(ps + C::kK), 16, 1024);
+      const uint64_t dv = sdesc(smem_u32(ps + C::kV), C::kBox, 1024);
+      if (role == kRoleS) {
         // S cursor: item ks, local step ns, global step gs
-        int ks = 0, ns = 0, gs = 0, its = prefill_item_of(0, num_items);
+        int ks = 0, ns = 0, gs = 0, its = prefill_item_of(pipe, num_items);
         int Ns = its >= 0 ? prefill_item(p, its).N : 0;
         while (its >= 0) {  // S(gs) = Q K(gs)^T into buffer gs % NS
           // P V(gs - NS) has read P from this buffer (its barrier last
@@ -399,13 +428,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           if (++ns == Ns) {  // this item's last S: its Q tile is free
             mma_commit(&q_empty[ks % C::kNQ]);
             ns = 0;
-            its = prefill_item_of(++ks, num_items);
+            its = prefill_item_of(++ks * C::kPipes + pipe, num_items);
             Ns = its >= 0 ? prefill_item(p, its).N : 0;
           }
         }
       } else {
         // P V cursor: item kp, local step np, global step gp
-        int kp = 0, np = 0, gp = 0, itp = prefill_item_of(0, num_items);
+        int kp = 0, np = 0, gp = 0, itp = prefill_item_of(pipe, num_items);
         int Np = itp >= 0 ? prefill_item(p, itp).N : 0;
         while (itp >= 0) {  // O(item) += P(gp) V(gp) once the softmax step is done
           const int st = gp % C::kST;
@@ -434,16 +463,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           ++gp;
           if (++np == Np) {
             np = 0;
-            itp = prefill_item_of(++kp, num_items);
+            itp = prefill_item_of(++kp * C::kPipes + pipe, num_items);
             Np = itp >= 0 ? prefill_item(p, itp).N : 0;
           }
         }
       }
     }
+  }
   } else {
+    if constexpr (DUAL) asm volatile("setmaxnreg.inc.sync.aligned.u32 200;" ::: "memory");
     // ================================================================ softmax
-    const int r = tid;  // query row = TMEM lane
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int r = tid & 127;  // query row = TMEM lane
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float sl2 = p.scale_log2;
     int g = 0;
     // The completion wait of a step's P stores and its p_full arrival are
@@ -470,7 +501,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     // P V(last - 1) has completed. After the last item the same waits hold
     // with S(last) seen (P V(last - 3) complete).
     auto epilogue = [&](int ke, long long base, int rows, float le, int last) {
-      if (last >= 1) wait(&o_done[(last - 1) & 1], ((last - 1) >> 1) & 1);
+      // (one pipeline per CTA: P V(last - 1) first, so that no wait here is on an
+      // ambiguous phase; two pipelines: P V(last) implies P V(last - 1), the
+      // same thread's earlier MMAs, and P V(last + 1) may have completed)
+      if (!DUAL && last >= 1) wait(&o_done[(last - 1) & 1], ((last - 1) >> 1) & 1);
       wait(&o_done[last & 1], (last >> 1) & 1);
       __syncwarp();
       tc_fence_after();
@@ -495,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         constexpr int kRowBytes = D * static_cast<int>(sizeof(OUT));
         constexpr int kChunks = kRowBytes / 16;
         constexpr int kPer32 = 32 * static_cast<int>(sizeof(OUT)) / 16;  // chunks per 32 values
-        uint8_t* stage = smem + C::kOut + warp * 32 * kRowBytes;
+        uint8_t* stage = ps + C::kOut + (warp & 3) * 32 * kRowBytes;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           float o[32];
@@ -521,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         constexpr int kRowsPer = 32 / kChunks;
         const int q = lane % kChunks;
         const uint8_t* src = stage + (lane / kChunks) * kRowBytes;
-        int row = warp * 32 + lane / kChunks;
+        int row = (warp & 3) * 32 + lane / kChunks;
         uint8_t* dst = reinterpret_cast<uint8_t*>(dst0 + row * row_stride) + (q << 4);
         const size_t dst_step = kRowsPer * row_stride * sizeof(OUT);
 #pragma unroll 1
@@ -560,8 +594,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     long long e_base = 0;                  // the output offset of its first row,
     float e_l = 0.f;                       // and this row's softmax sum
     const uint32_t ninf = __float_as_uint(-INFINITY);
+    int sj = 0;        // g % NS, kept incrementally (no division on the loop head)
+    uint32_t sph = 0;  // (g / NS) & 1
     for (int k = 0;; ++k) {
-      const int it = prefill_item_of(k, num_items);
+      const int it = prefill_item_of(k * C::kPipes + pipe, num_items);
       if (it < 0) break;
       const PrefillItem w = prefill_item(p, it);
       const uint32_t o_addr = lane_addr + C::kO + D * (k % C::kNO);
@@ -569,82 +605,163 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const int first_r = p.sliding > 0 ? max(0, pr - p.sliding + 1) : 0;
       float m_run = -INFINITY, l_run = 0.f;
       for (int n = 0; n < w.N; ++n, ++g) {
-        const int j = g % NS;
+        const int j = sj;
         const uint32_t buf = lane_addr + 128 * j;
-        wait(&s_full[j], (g / NS) & 1);
+        wait(&s_full[j], sph);
+        if (++sj == NS) {
+          sj = 0;
+          sph ^= 1u;
+        }
         if (tid == 0) PTRACE(0, g);
         __syncwarp();
         tc_fence_after();
         if (tid == 0) PTRACE(1, g);
-        uint32_t sv[128];
-        tmem_ld64x(buf, *reinterpret_cast<uint32_t(*)[64]>(&sv[0]));
-        tmem_ld64x(buf + 64, *reinterpret_cast<uint32_t(*)[64]>(&sv[64]));
-        if (tid == 0) PTRACE(2, g);
-        release_p();  // the previous step's P (its P V may now be issued)
-        const int tok0 = (w.j0 + n) * kT;
-        const bool masked = tok0 + kT - 1 > pr || tok0 < first_r;
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (masked) {
-          // valid columns [lo, hi] (lo <= hi: first_r <= pr); one unsigned
-          // compare and a select per column, no branch
+        // Row maximum of the step -> moves the row's reference maximum (and
+        // rescales O in TMEM) when exceeded by more than 2^8; returns the
+        // maximum the exponentials subtract.
+        auto apply_max = [&](float m_tile) -> float {
+          const bool grow = m_tile > m_run + kRescaleLog2;
+          if (__any_sync(0xffffffffu, grow)) {
+            const float m_new = grow ? m_tile : m_run;
+            // 0 while the row has seen no unmasked token (O and l are still zero), 1 when unchanged
+            const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - m_new);
+            if (n > 0) {  // rescale O in TMEM once P V(g-1) finished
+              wait(&o_done[(g - 1) & 1], ((g - 1) >> 1) & 1);
+              __syncwarp();
+              tc_fence_after();
+#pragma unroll
+              for (int c = 0; c < D / 32; ++c) {
+                float o[32];
+                uint32_t u[32];
+                tmem_ld32(o_addr + 32 * c, o);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * alpha);
+                tmem_st32(o_addr + 32 * c, u);
+              }
+            }
+            l_run *= alpha;
+            m_run = m_new;
+          }
+          return m_run == -INFINITY ? 0.f : m_run;
+        };
+        if constexpr (!DUAL) {
+          uint32_t sv[128];
+          tmem_ld64x(buf, *reinterpret_cast<uint32_t(*)[64]>(&sv[0]));
+          tmem_ld64x(buf + 64, *reinterpret_cast<uint32_t(*)[64]>(&sv[64]));
+          if (tid == 0) PTRACE(2, g);
+          release_p();  // the previous step's P (its P V may now be issued)
+          const int tok0 = (w.j0 + n) * kT;
+          const bool masked = tok0 + kT - 1 > pr || tok0 < first_r;
+          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+          if (masked) {
+            // valid columns [lo, hi] (lo <= hi: first_r <= pr); one unsigned
+            // compare and a select per column, no branch
+            const int lo = first_r - tok0;
+            const uint32_t span = static_cast<uint32_t>(pr - first_r);
+#pragma unroll
+            for (int i = 0; i < 128; ++i) sv[i] = static_cast<uint32_t>(i - lo) <= span ? sv[i] : ninf;
+          }
+#pragma unroll
+          for (int i = 0; i < 128; i += 8) {  // four independent chains of three-input maxima
+            mx[0] = fmax3(mx[0], __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
+            mx[1] = fmax3(mx[1], __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]));
+            mx[2] = fmax3(mx[2], __uint_as_float(sv[i + 4]), __uint_as_float(sv[i + 5]));
+            mx[3] = fmax3(mx[3], __uint_as_float(sv[i + 6]), __uint_as_float(sv[i + 7]));
+          }
+          const float mu = apply_max(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2);
+          // x = S * scale_log2 - mu and the row sum, two columns per instruction
+          const uint64_t sl2x2 = pack_f32x2(sl2, sl2), nmu2 = pack_f32x2(-mu, -mu);
+          uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t pk[32];
+#pragma unroll
+            for (int i = 0; i < 64; i += 2) {
+              const int kc = 64 * c + i;
+              const bool poly = poly_pair(kc / 2);
+              float x0, x1;
+              fma_f32x2(__uint_as_float(sv[kc]), __uint_as_float(sv[kc + 1]), sl2x2, nmu2, x0, x1);
+              const float e0 = poly ? ex2_poly(x0) : ex2(x0);
+              const float e1 = poly ? ex2_poly(x1) : ex2(x1);
+              add_f32x2(sum2[(i >> 1) & 3], e0, e1);
+              pk[i / 2] = pack_half2(e0, e1);
+            }
+            tmem_st32(buf + 32 * c, pk);
+          }
+          l_run += (sum_f32x2(sum2[0]) + sum_f32x2(sum2[1])) + (sum_f32x2(sum2[2]) + sum_f32x2(sum2[3]));
+        } else {
+          // Half width (two pipelines share the SM's registers): columns 0..63
+          // stay in registers, the maximum of 64..127 is taken in 32-column
+          // pieces; after the exponentials of the first half (P over S columns
+          // 0..31, already read) the second half is reloaded (P over S columns
+          // 32..63, also already read).
+          const int tok0 = (w.j0 + n) * kT;
+          const bool masked = tok0 + kT - 1 > pr || tok0 < first_r;
           const int lo = first_r - tok0;
           const uint32_t span = static_cast<uint32_t>(pr - first_r);
+          uint32_t sa[64];
+          tmem_ld64x(buf, sa);
+          if (tid == 0) PTRACE(2, g);
+          if (masked) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) sv[i] = static_cast<uint32_t>(i - lo) <= span ? sv[i] : ninf;
-        }
+            for (int i = 0; i < 64; ++i) sa[i] = static_cast<uint32_t>(i - lo) <= span ? sa[i] : ninf;
+          }
+          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < 128; i += 8) {  // four independent chains of three-input maxima
-          mx[0] = fmax3(mx[0], __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
-          mx[1] = fmax3(mx[1], __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]));
-          mx[2] = fmax3(mx[2], __uint_as_float(sv[i + 4]), __uint_as_float(sv[i + 5]));
-          mx[3] = fmax3(mx[3], __uint_as_float(sv[i + 6]), __uint_as_float(sv[i + 7]));
-        }
-        const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
-        const bool grow = m_tile > m_run + kRescaleLog2;
-        if (__any_sync(0xffffffffu, grow)) {
-          const float m_new = grow ? m_tile : m_run;
-          // 0 while the row has seen no unmasked token (O and l are still zero), 1 when unchanged
-          const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - m_new);
-          if (n > 0) {  // rescale O in TMEM once P V(g-1) finished
-            wait(&o_done[(g - 1) & 1], ((g - 1) >> 1) & 1);
-            __syncwarp();
-            tc_fence_after();
+          for (int i = 0; i < 64; i += 8) {
+            mx[0] = fmax3(mx[0], __uint_as_float(sa[i]), __uint_as_float(sa[i + 1]));
+            mx[1] = fmax3(mx[1], __uint_as_float(sa[i + 2]), __uint_as_float(sa[i + 3]));
+            mx[2] = fmax3(mx[2], __uint_as_float(sa[i + 4]), __uint_as_float(sa[i + 5]));
+            mx[3] = fmax3(mx[3], __uint_as_float(sa[i + 6]), __uint_as_float(sa[i + 7]));
+          }
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-              float o[32];
-              uint32_t u[32];
-              tmem_ld32(o_addr + 32 * c, o);
+          for (int c = 0; c < 2; ++c) {
+            float t[32];
+            tmem_ld32(buf + 64 + 32 * c, t);
+            if (masked) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * alpha);
-              tmem_st32(o_addr + 32 * c, u);
+              for (int i = 0; i < 32; ++i)
+                t[i] = static_cast<uint32_t>(64 + 32 * c + i - lo) <= span ? t[i] : -INFINITY;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              mx[0] = fmax3(mx[0], t[i], t[i + 1]);
+              mx[1] = fmax3(mx[1], t[i + 2], t[i + 3]);
+              mx[2] = fmax3(mx[2], t[i + 4], t[i + 5]);
+              mx[3] = fmax3(mx[3], t[i + 6], t[i + 7]);
             }
           }
-          l_run *= alpha;
-          m_run = m_new;
-        }
-        const float mu = m_run == -INFINITY ? 0.f : m_run;
-        // x = S * scale_log2 - mu and the row sum, two columns per instruction
-        const uint64_t sl2x2 = pack_f32x2(sl2, sl2), nmu2 = pack_f32x2(-mu, -mu);
-        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+          const float mu = apply_max(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2);
+          const uint64_t sl2x2 = pack_f32x2(sl2, sl2), nmu2 = pack_f32x2(-mu, -mu);
+          uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+          auto exps = [&](const uint32_t (&v)[64], int c0, uint32_t dst) {
+            uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t pk[32];
+            for (int i = 0; i < 64; i += 2) {
+              const bool poly = poly_pair((c0 + i) / 2);
+              float x0, x1;
+              fma_f32x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), sl2x2, nmu2, x0, x1);
+              const float e0 = poly ? ex2_poly(x0) : ex2(x0);
+              const float e1 = poly ? ex2_poly(x1) : ex2(x1);
+              add_f32x2(sum2[(i >> 1) & 3], e0, e1);
+              pk[i / 2] = pack_half2(e0, e1);
+            }
+            tmem_st32(dst, pk);
+          };
+          exps(sa, 0, buf);
+          tmem_ld64x(buf + 64, sa);
+          if (masked) {
 #pragma unroll
-          for (int i = 0; i < 64; i += 2) {
-            const int kc = 64 * c + i;
-            const bool poly = poly_pair(kc / 2);
-            float x0, x1;
-            fma_f32x2(__uint_as_float(sv[kc]), __uint_as_float(sv[kc + 1]), sl2x2, nmu2, x0, x1);
-            const float e0 = poly ? ex2_poly(x0) : ex2(x0);
-            const float e1 = poly ? ex2_poly(x1) : ex2(x1);
-            add_f32x2(sum2[(i >> 1) & 3], e0, e1);
-            pk[i / 2] = pack_half2(e0, e1);
+            for (int i = 0; i < 64; ++i) sa[i] = static_cast<uint32_t>(64 + i - lo) <= span ? sa[i] : ninf;
           }
-          tmem_st32(buf + 32 * c, pk);
+          exps(sa, 64, buf + 32);
+          l_run += (sum_f32x2(sum2[0]) + sum_f32x2(sum2[1])) + (sum_f32x2(sum2[2]) + sum_f32x2(sum2[3]));
         }
-        l_run += (sum_f32x2(sum2[0]) + sum_f32x2(sum2[1])) + (sum_f32x2(sum2[2]) + sum_f32x2(sum2[3]));
         if (lane == 0) PTRACE(3 + warp, g);
         pend_j = j;
+        // two pipelines: the next S of this pipeline waits for this step's P V
+        // (one S buffer), so P is released at once
+        if constexpr (DUAL) release_p();
         if (n == 0 && e_k >= 0) {  // the previous item's epilogue (its last P V is done by now)
           epilogue(e_k, e_base, e_rows, e_l, e_last);
           e_k = -1;
@@ -661,9 +778,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == C::kAllocWarp) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(*tmem_slot), "r"(C::kCols) : "memory");
   }
 }
 
@@ -678,9 +795,9 @@ CUresult make_map(const tla_layer* L, void* base, uint64_t rows, uint64_t planes
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-template <int D, typename OUT>
+template <int D, typename OUT, bool DUAL>
 cudaError_t set_smem() {
-  return raise_smem_limit(reinterpret_cast<const void*>(prefill_tc_kernel<D, OUT>), PCfg<D>::kSmem);
+  return raise_smem_limit(reinterpret_cast<const void*>(prefill_tc_kernel<D, OUT, DUAL>), PCfg<D, DUAL>::kSmem);
 }
 
 }  // namespace
@@ -699,11 +816,12 @@ cudaError_t prefill_fast_configure(tla_layer* L) {
       make_map(L, L->v_cache, L->max_tokens, planes, &L->tmap_v128) != CUDA_SUCCESS)
     return cudaSuccess;
   cudaError_t e;
-  if (L->D == 64) {
-    e = L->io_fp32 ? set_smem<64, float>() : set_smem<64, __half>();
-    L->prefill_smem = PCfg<64>::kSmem;
+  if (L->D == 64) {  // two pipelines per CTA
+    constexpr bool kDual = TLA_PREFILL_DUAL != 0;
+    e = L->io_fp32 ? set_smem<64, float, kDual>() : set_smem<64, __half, kDual>();
+    L->prefill_smem = PCfg<64, kDual>::kSmem;
   } else {
-    e = L->io_fp32 ? set_smem<128, float>() : set_smem<128, __half>();
+    e = L->io_fp32 ? set_smem<128, float, false>() : set_smem<128, __half, false>();
     L->prefill_smem = PCfg<128>::kSmem;
   }
   if (e != cudaSuccess) return e;
@@ -742,15 +860,18 @@ cudaError_t launch_prefill_attention(const tla_layer* L, const int32_t* start, c
   const int items = p.num_m * batch * L->Hq;
   const dim3 grid(static_cast<unsigned>(items < L->ctx->sm_count ? items : L->ctx->sm_count));
   if (L->D == 64) {
+    constexpr bool kDual = TLA_PREFILL_DUAL != 0;
+    using C = PCfg<64, kDual>;
     if (L->io_fp32)
-      return launch_pdl(prefill_tc_kernel<64, float>, grid.x, kThreads, PCfg<64>::kSmem, stream, p);
+      return launch_pdl(prefill_tc_kernel<64, float, kDual>, grid.x, C::kThreads, C::kSmem, stream, p);
     else
-      return launch_pdl(prefill_tc_kernel<64, __half>, grid.x, kThreads, PCfg<64>::kSmem, stream, p);
+      return launch_pdl(prefill_tc_kernel<64, __half, kDual>, grid.x, C::kThreads, C::kSmem, stream, p);
   } else {
+    using C = PCfg<128>;
     if (L->io_fp32)
-      return launch_pdl(prefill_tc_kernel<128, float>, grid.x, kThreads, PCfg<128>::kSmem, stream, p);
+      return launch_pdl(prefill_tc_kernel<128, float, false>, grid.x, C::kThreads, C::kSmem, stream, p);
     else
-      return launch_pdl(prefill_tc_kernel<128, __half>, grid.x, kThreads, PCfg<128>::kSmem, stream, p);
+      return launch_pdl(prefill_tc_kernel<128, __half, false>, grid.x, C::kThreads, C::kSmem, stream, p);
   }
   return cudaGetLastError();
 }

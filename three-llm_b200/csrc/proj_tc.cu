@@ -58,6 +58,12 @@ struct ProjParams {
   // words in that rank's exchange buffer, slot [this rank], first half
   ExchangeDev x;
   int cols;
+  // split-K (few rows, decode): ksplit CTAs share a tile; each adds its fp32
+  // partial into ws [rows][N] and the last one (tile_cnt ticket) runs the
+  // epilogue from ws and zeroes it again
+  int ksplit;
+  float* ws;
+  int* tile_cnt;  // [m_tiles * (N / NT)], zero between launches
 };
 
 __host__ __device__ inline int stage_bytes(int NT) { return kXStage + (NT / 64) * kWBox; }
@@ -79,9 +85,14 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int m0 = (static_cast<int>(blockIdx.x) % p.m_tiles) * 128;
-  const int n0 = (static_cast<int>(blockIdx.x) / p.m_tiles) * p.NT;
-  const int kchunks = (p.K + 63) / 64;
+  const int n_tiles = p.N / p.NT;
+  const int tile = static_cast<int>(blockIdx.x) % (p.m_tiles * n_tiles);
+  const int ks = static_cast<int>(blockIdx.x) / (p.m_tiles * n_tiles);
+  const int m0 = (tile % p.m_tiles) * 128;
+  const int n0 = (tile / p.m_tiles) * p.NT;
+  const int kc_all = (p.K + 63) / 64;
+  const int kc0 = (ks * kc_all) / p.ksplit, kc1 = ((ks + 1) * kc_all) / p.ksplit;
+  const int kchunks = kc1 - kc0;  // this CTA's 64-element chunks of the reduction dim
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
@@ -119,8 +130,9 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
       if (*abort_flag) continue;
       uint8_t* st = smem + s * sb;
       mbar_arrive_expect_tx(&full[s], sb);
-      tma_load_2d(st, &p.tm_x, &full[s], c * 64, m0);
-      for (int i = 0; i < p.NT / 64; ++i) tma_load_2d(st + kXStage + i * kWBox, &p.tm_w, &full[s], n0 + 64 * i, c * 64);
+      const int kx = (kc0 + c) * 64;
+      tma_load_2d(st, &p.tm_x, &full[s], kx, m0);
+      for (int i = 0; i < p.NT / 64; ++i) tma_load_2d(st + kXStage + i * kWBox, &p.tm_w, &full[s], n0 + 64 * i, kx);
     }
     for (int c = kchunks > p.stages ? kchunks - p.stages : 0; c < kchunks; ++c)  // no copies in flight at exit
       wait(&full[c % p.stages], (c / p.stages) & 1);
@@ -153,6 +165,57 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
   const int r = tid, row = m0 + r;
   const bool valid = row < p.rows;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  if (p.ksplit > 1) {
+    // add this CTA's partial tile into the workspace; the last CTA of the tile
+    // goes on to the epilogue, reading the complete sums from the workspace
+    for (int c = 0; c < p.NT / 32; ++c) {
+      float v[32];
+      tmem_ld32(lane_base + 32 * c, v);
+      if (!valid) continue;
+      float* dst = p.ws + static_cast<size_t>(row) * p.N + n0 + 32 * c;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * i), "f"(v[4 * i]),
+                     "f"(v[4 * i + 1]), "f"(v[4 * i + 2]), "f"(v[4 * i + 3])
+                     : "memory");
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) epoch_s = atomicAdd(p.tile_cnt + tile, 1) == p.ksplit - 1 ? 1 : 0;
+    __syncthreads();
+    const bool last = epoch_s != 0;
+    __syncthreads();  // epoch_s is reused by the push epilogue
+    if (!last) {
+      tc_fence_before();
+      __syncthreads();
+      if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
+      }
+      return;
+    }
+    __threadfence();
+    if (tid == 0) p.tile_cnt[tile] = 0;
+  }
+  // The tile's accumulator columns [c0, c0 + 32) of this thread's row: from
+  // TMEM (warp-collective), or, split-K, from the workspace, which is zeroed
+  // behind the read for the next launch.
+  auto load_acc = [&](int c0, float (&v)[32]) {
+    if (p.ksplit == 1) {
+      tmem_ld32(lane_base + c0, v);
+    } else if (valid) {
+      float4* src = reinterpret_cast<float4*>(p.ws + static_cast<size_t>(row) * p.N + n0 + c0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 q = __ldcg(src + i);
+        v[4 * i] = q.x;
+        v[4 * i + 1] = q.y;
+        v[4 * i + 2] = q.z;
+        v[4 * i + 3] = q.w;
+        __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
+      }
+    }
+  };
   if (p.mode == kQkvDecode || p.mode == kQkvPrefill) {
     // ---------------------------------------------------------------- QKV epilogue
     const LayerArgs& a = p.a;
@@ -186,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float v[32];
-        tmem_ld32(lane_base + j * D + 32 * c, v);  // warp-collective: every lane loads
+        load_acc(j * D + 32 * c, v);  // TMEM: warp-collective, every lane loads
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float x = v[i] + (p.bias ? __ldg(p.bias + hh * D + 32 * c + i) : 0.f);
@@ -246,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
                          (n0 - owner * p.cols);
     for (int c = 0; c < p.NT / 32; ++c) {
       float v[32];
-      tmem_ld32(lane_base + 32 * c, v);
+      load_acc(32 * c, v);
       if (!valid) continue;
 #pragma unroll
       for (int i = 0; i < 16; ++i)
@@ -257,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
     // ---------------------------------------------------------------- output projection epilogue
     for (int c = 0; c < p.NT / 32; ++c) {
       float v[32];
-      tmem_ld32(lane_base + 32 * c, v);
+      load_acc(32 * c, v);
       if (!valid) continue;
       const int col = n0 + 32 * c;
       const size_t o = static_cast<size_t>(row) * p.N + col;
@@ -335,9 +398,25 @@ int choose_nt(int N, int unit, int m_tiles, int sms) {
 }
 
 template <int D>
-cudaError_t launch_proj_t(const tla_ctx* ctx, ProjParams& p, cudaStream_t stream) {
+cudaError_t launch_proj_t(tla_ctx* ctx, ProjParams& p, cudaStream_t stream) {
   const int sb = stage_bytes(p.NT);
-  int stages = (200 * 1024) / sb;
+  const int n_tiles = p.N / p.NT, tiles = p.m_tiles * n_tiles, kc_all = (p.K + 63) / 64;
+  // Few tiles (decode rows): split the reduction dimension so that about two
+  // CTAs per SM stream the weights (4 stages each, so two fit on an SM).
+  p.ksplit = 1;
+  if (tiles < ctx->sm_count && kc_all >= 8) {
+    int ks = (2 * ctx->sm_count + tiles - 1) / tiles;
+    if (ks > kc_all / 4) ks = kc_all / 4;
+    if (ks > 1) {
+      const size_t ws = static_cast<size_t>(p.rows) * p.N;
+      if (ensure_proj_workspace(ctx, ws, tiles) == cudaSuccess) {
+        p.ksplit = ks;
+        p.ws = ctx->d_proj_ws;
+        p.tile_cnt = ctx->d_proj_cnt;
+      }
+    }
+  }
+  int stages = p.ksplit > 1 ? 4 : (200 * 1024) / sb;
   if (stages > 8) stages = 8;
   if (stages < 2) stages = 2;
   p.stages = stages;
@@ -347,8 +426,7 @@ cudaError_t launch_proj_t(const tla_ctx* ctx, ProjParams& p, cudaStream_t stream
   const void* k = reinterpret_cast<const void*>(proj_tc_kernel<D>);
   cudaError_t e = raise_smem_limit(k, smem);
   if (e != cudaSuccess) return e;
-  const int n_tiles = p.N / p.NT;
-  return launch_pdl(proj_tc_kernel<D>, static_cast<unsigned>(p.m_tiles * n_tiles), kThreads, smem, stream, p);
+  return launch_pdl(proj_tc_kernel<D>, static_cast<unsigned>(tiles * p.ksplit), kThreads, smem, stream, p);
 }
 
 // Second half of the head-sharded output projection, one 128-thread CTA per SM
@@ -370,18 +448,17 @@ __global__ void __launch_bounds__(128) out_allreduce_kernel(ExchangeDev x, int r
   const size_t half_words = static_cast<size_t>(rows) * cols;  // second half of a slot
   const int pairs = static_cast<int>(half_words / 2);
   const int stride = static_cast<int>(gridDim.x * blockDim.x);
-  auto wait_words = [&](uint4 (&w)[kXchMaxRanks], size_t word, int only) {
-    // only < 0: every rank's slot; else just slot `only`
+  auto wait_words = [&](uint4 (&w)[kXchMaxRanks], size_t word) {  // every rank's word of a pair
     auto load = [&](int r) { return xch_ld_v4(mine + (static_cast<size_t>(r) * x.slot_words + word) * 8); };
 #pragma unroll
     for (int r = 0; r < kXchMaxRanks; ++r)
-      if (r < x.ranks && (only < 0 || r == only)) w[r] = load(r);
+      if (r < x.ranks) w[r] = load(r);
     unsigned long long t0 = 0;
     for (;;) {
       bool done = true;
 #pragma unroll
       for (int r = 0; r < kXchMaxRanks; ++r)
-        if (r < x.ranks && (only < 0 || r == only) && (w[r].y != epoch || w[r].w != epoch)) {
+        if (r < x.ranks && (w[r].y != epoch || w[r].w != epoch)) {
           done = false;
           w[r] = load(r);
         }
@@ -406,7 +483,7 @@ __global__ void __launch_bounds__(128) out_allreduce_kernel(ExchangeDev x, int r
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
     const int row = (2 * i) / cols, lc = 2 * i - row * cols, col = x.rank * cols + lc;
     uint4 w[kXchMaxRanks];
-    wait_words(w, static_cast<size_t>(2 * i), -1);
+    wait_words(w, static_cast<size_t>(2 * i));
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int r = 0; r < kXchMaxRanks; ++r)
@@ -440,9 +517,21 @@ __global__ void __launch_bounds__(128) out_allreduce_kernel(ExchangeDev x, int r
     if (q == x.rank) continue;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
       const int row = (2 * i) / cols, lc = 2 * i - row * cols;
-      uint4 w[kXchMaxRanks];
-      wait_words(w, half_words + 2 * i, q);
-      store(row, q * cols + lc, __uint_as_float(w[q].x), __uint_as_float(w[q].z));
+      const uint8_t* src = mine + (static_cast<size_t>(q) * x.slot_words + half_words + 2 * i) * 8;
+      uint4 w = xch_ld_v4(src);
+      unsigned long long t0 = 0;
+      while ((w.y != epoch || w.w != epoch) && *abort_p != static_cast<int>(epoch)) {
+        const unsigned long long now = globaltimer();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kWaitLimitNs) {
+          report_error(error, TLA_ERR_TIMEOUT);
+          *abort_p = static_cast<int>(epoch);
+          break;
+        }
+        w = xch_ld_v4(src);
+      }
+      store(row, q * cols + lc, __uint_as_float(w.x), __uint_as_float(w.z));
     }
   }
   xch_finish(x, epoch);
@@ -450,7 +539,7 @@ __global__ void __launch_bounds__(128) out_allreduce_kernel(ExchangeDev x, int r
 
 }  // namespace
 
-cudaError_t launch_out_proj_allreduce(const tla_ctx* ctx, const ExchangeDev& x, const void* attn,
+cudaError_t launch_out_proj_allreduce(tla_ctx* ctx, const ExchangeDev& x, const void* attn,
                                       const void* weight, const float* bias, const void* residual, bool f32, void* y,
                                       int rows, int in_features, int hidden, cudaStream_t stream) {
   ProjParams p{};
@@ -503,7 +592,7 @@ cudaError_t launch_qkv_proj(const tla_layer* L, const void* x, const void* weigh
   return L->D == 64 ? launch_proj_t<64>(L->ctx, p, stream) : launch_proj_t<128>(L->ctx, p, stream);
 }
 
-cudaError_t launch_out_proj(const tla_ctx* ctx, const void* attn, const void* weight, const float* bias,
+cudaError_t launch_out_proj(tla_ctx* ctx, const void* attn, const void* weight, const float* bias,
                             const void* residual, bool residual_f32, void* y, bool y_f32, int rows, int in_features,
                             int hidden, cudaStream_t stream) {
   ProjParams p{};

@@ -74,6 +74,30 @@ cudaError_t raise_smem_limit(const void* kernel, int bytes) {
   return e;
 }
 
+cudaError_t ensure_proj_workspace(tla_ctx* ctx, size_t floats, size_t tiles) {
+  if (floats <= ctx->proj_ws_floats && tiles <= ctx->proj_cnt_count) return cudaSuccess;
+  cudaError_t e = cudaSuccess;
+  if (floats > ctx->proj_ws_floats) {
+    cudaFree(ctx->d_proj_ws);
+    ctx->d_proj_ws = nullptr;
+    ctx->proj_ws_floats = 0;
+    e = cudaMalloc(&ctx->d_proj_ws, floats * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_proj_ws, 0, floats * sizeof(float));
+    if (e != cudaSuccess) return e;
+    ctx->proj_ws_floats = floats;
+  }
+  if (tiles > ctx->proj_cnt_count) {
+    cudaFree(ctx->d_proj_cnt);
+    ctx->d_proj_cnt = nullptr;
+    ctx->proj_cnt_count = 0;
+    e = cudaMalloc(&ctx->d_proj_cnt, tiles * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_proj_cnt, 0, tiles * sizeof(int));
+    if (e != cudaSuccess) return e;
+    ctx->proj_cnt_count = tiles;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t cached_occupancy(const void* kernel, int threads, int smem, int* blocks) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -242,6 +266,8 @@ int tla_destroy(tla_ctx* ctx) {
   cudaFree(ctx->d_partials);
   cudaFree(ctx->d_counters);
   cudaFree(ctx->d_qscratch);
+  cudaFree(ctx->d_proj_ws);
+  cudaFree(ctx->d_proj_cnt);
   delete ctx;
   return TLA_OK;
 }
@@ -261,6 +287,10 @@ int tla_get_error(tla_ctx* ctx, int reset) {
     // the next launch's tickets need every counter at zero.
     if (e == cudaSuccess && v != 0 && ctx->d_counters)
       e = cudaMemset(ctx->d_counters, 0, ctx->counter_count * sizeof(int32_t));
+    if (e == cudaSuccess && v != 0 && ctx->d_proj_ws)
+      e = cudaMemset(ctx->d_proj_ws, 0, ctx->proj_ws_floats * sizeof(float));
+    if (e == cudaSuccess && v != 0 && ctx->d_proj_cnt)
+      e = cudaMemset(ctx->d_proj_cnt, 0, ctx->proj_cnt_count * sizeof(int));
     if (e != cudaSuccess) return from_cuda(e);
   }
   return v;

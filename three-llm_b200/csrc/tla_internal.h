@@ -22,6 +22,12 @@ struct tla_ctx {
   // prefill / generic-path query scratch (rotated queries)
   void* d_qscratch = nullptr;
   size_t qscratch_bytes = 0;
+  // split-K projection workspace: fp32 partial sums and per-tile tickets,
+  // zero between launches
+  float* d_proj_ws = nullptr;
+  size_t proj_ws_floats = 0;
+  int* d_proj_cnt = nullptr;
+  size_t proj_cnt_count = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
 };
 
@@ -148,6 +154,8 @@ cudaError_t launch_prefill_attention(const tla_layer* L, const int32_t* start, c
 // in the cache (the fused QKV projection's output).
 cudaError_t launch_decode_fast_qrot(const tla_layer* L, const __half* qrot, const int32_t* positions,
                                     const void* gate, void* out, int batch, cudaStream_t stream);
+// Grows the context's split-K workspace (zeroed) to at least the given size.
+cudaError_t ensure_proj_workspace(tla_ctx* ctx, size_t floats, size_t tiles);
 // Tensor-core projections (proj_tc.cu). QKV: x [rows][hidden] fp16 times
 // weight [hidden][(Hq+2Hk)D] fp16 (+ bias), epilogue QK-norm / RoPE / append,
 // rotated queries to qout. Output projection: y = residual + attn W + bias
@@ -158,10 +166,10 @@ cudaError_t launch_qkv_proj(const tla_layer* L, const void* x, const void* weigh
 // Head-sharded output projection: this rank's partial product tiles are stored
 // over NVLink into the exchange buffer of the rank owning their columns, then
 // one kernel sums the owned block, adds bias + residual and all-gathers.
-cudaError_t launch_out_proj_allreduce(const tla_ctx* ctx, const ExchangeDev& x, const void* attn,
+cudaError_t launch_out_proj_allreduce(tla_ctx* ctx, const ExchangeDev& x, const void* attn,
                                       const void* weight, const float* bias, const void* residual, bool f32, void* y,
                                       int rows, int in_features, int hidden, cudaStream_t stream);
-cudaError_t launch_out_proj(const tla_ctx* ctx, const void* attn, const void* weight, const float* bias,
+cudaError_t launch_out_proj(tla_ctx* ctx, const void* attn, const void* weight, const float* bias,
                             const void* residual, bool residual_f32, void* y, bool y_f32, int rows, int in_features,
                             int hidden, cudaStream_t stream);
 
