@@ -42,7 +42,9 @@ typedef enum tla_status {
   TLA_ERR_TIMEOUT = -13,      /* device-reported: a bounded in-kernel wait expired */
   TLA_ERR_NO_DEVICE = -14,
   TLA_ERR_SHARED = -15,       /* operation not allowed on a layer that borrows another's cache */
-  TLA_ERR_SCRATCH_LIMIT = -16 /* request exceeds the fixed scratch of tla_decode_noalloc */
+  TLA_ERR_SCRATCH_LIMIT = -16, /* request exceeds the fixed scratch of tla_decode_noalloc */
+  TLA_ERR_BOUNDS = -17         /* device-reported, bounds-check builds only: an index outside its buffer
+                                  (the access was skipped) */
 } tla_status;
 
 /* RoPE scaling: RopeScalingConfig | YarnRoPEConfig (packages/three-llm/src/types.ts:245-256). */

@@ -18,7 +18,7 @@ STATUS = {
     -4: "TLA_ERR_ROPE_FACTOR", -5: "TLA_ERR_YARN_RANGE", -6: "TLA_ERR_YARN_FACTOR", -7: "TLA_ERR_LLAMA3_RANGE",
     -8: "TLA_ERR_ROTARY_DIM", -9: "TLA_ERR_UNSUPPORTED", -10: "TLA_ERR_CUDA", -11: "TLA_ERR_OUT_OF_MEMORY",
     -12: "TLA_ERR_POSITION", -13: "TLA_ERR_TIMEOUT", -14: "TLA_ERR_NO_DEVICE", -15: "TLA_ERR_SHARED",
-    -16: "TLA_ERR_SCRATCH_LIMIT",
+    -16: "TLA_ERR_SCRATCH_LIMIT", -17: "TLA_ERR_BOUNDS",
 }
 ROPE_TYPES = {"default": 0, "none": 0, "linear": 1, "yarn": 2, "llama3": 3}
 FLAG_OFFSET_RMS_NORM = 1 << 0

@@ -42,6 +42,12 @@ constexpr int kMaxBatch = 1024;      // prefix table in shared memory
 
 // Pipeline depth per head_dim: at 2 resident CTAs per SM a 4-stage (D=64) or
 // 2-stage (D=128) ring keeps 64-128 KB of K/V in flight per SM.
+// A pair split over more than this many CTAs (segments) is merged by
+// decode_merge_kernel instead of by the last CTA in the decode kernel.
+#ifndef TLA_DEFER_MERGE_SEGMENTS
+#define TLA_DEFER_MERGE_SEGMENTS 4
+#endif
+
 #ifndef TLA_DECODE_STAGES_D64
 #define TLA_DECODE_STAGES_D64 4
 #endif
@@ -105,6 +111,7 @@ struct DecodeParams {
                        // (which also appended the new K/V): no QK-norm / RoPE / append here
   float* scratch;      // [grid][2][G][D + 2]
   int32_t* counters;   // [B * Hk], zero between launches
+  long long scratch_floats, counter_count;  // extents (bounds-check builds)
   int batch, slot_offset, local_tokens, append;
   int defer_merge;  // 1: split pairs are merged by decode_merge_kernel instead of the last CTA
 };
@@ -574,9 +581,12 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     named_barrier_sync(1, 128);
     if (has_new && tid < D / 8) {  // append to the cache (copy-KV, TSLAttention.ts:280-281)
       const size_t base = ((static_cast<size_t>(b) * Hk + kvh) * a.max_tokens + slot_new) * D + tid * 8;
-      reinterpret_cast<uint4*>(static_cast<__half*>(a.k_cache) + base)[0] = reinterpret_cast<const uint4*>(newkv)[tid];
-      reinterpret_cast<uint4*>(static_cast<__half*>(a.v_cache) + base)[0] =
-          reinterpret_cast<const uint4*>(newkv + D)[tid];
+      if (TLA_IN_BOUNDS(base + 7, static_cast<long long>(a.max_batch) * Hk * a.max_tokens * D, a.error)) {
+        reinterpret_cast<uint4*>(static_cast<__half*>(a.k_cache) + base)[0] =
+            reinterpret_cast<const uint4*>(newkv)[tid];
+        reinterpret_cast<uint4*>(static_cast<__half*>(a.v_cache) + base)[0] =
+            reinterpret_cast<const uint4*>(newkv + D)[tid];
+      }
     }
     if (tid == 0 && it == 0) DTRACE(12);
     uint32_t qa[D / 16][4];
@@ -749,7 +759,10 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         }
       }
       if (!whole) {
-        mine[i] = v;
+        if (TLA_IN_BOUNDS((static_cast<long long>(cta) * 2 + slot) * G * (D + 2) + i, p.scratch_floats, a.error))
+          mine[i] = v;
+      } else if (!TLA_IN_BOUNDS(static_cast<long long>(b) * Hq + kvh * G + r, static_cast<long long>(p.batch) * Hq,
+                                a.error)) {
       } else if (p.partial_out) {
         p.partial_out[(static_cast<size_t>(b) * Hq + kvh * G + r) * (D + 2) + e] = v;
       } else if (e >= 2) {
@@ -772,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
       named_barrier_sync(1, 128);
       const int pair = b * Hk + kvh;
       if (tid == 0) {
-        const int old = atomicAdd(&p.counters[pair], n);
+        const int old = TLA_IN_BOUNDS(pair, p.counter_count, a.error) ? atomicAdd(&p.counters[pair], n) : -1;
         flags[1] = (old + n == tiles) ? 1 : 0;
       }
       named_barrier_sync(1, 128);
@@ -796,7 +809,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
         named_barrier_sync(1, 128);
         auto seg = [&](int c) -> const float* {  // this pair's triple block in CTA c's scratch, or null
           const int sl = slot_of[c - c0];
-          return sl < 0 ? nullptr : p.scratch + static_cast<size_t>(sl) * G * (D + 2);
+          if (sl < 0 || !TLA_IN_BOUNDS((static_cast<long long>(sl) + 1) * G * (D + 2) - 1, p.scratch_floats, a.error))
+            return nullptr;
+          return p.scratch + static_cast<size_t>(sl) * G * (D + 2);
         };
         float lm[16], ll[16];
 #pragma unroll
@@ -870,7 +885,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
             static_cast<IO*>(p.out)[oi] = from_f32<IO>(val);
           }
         }
-        if (tid == 0) p.counters[pair] = 0;
+        if (tid == 0 && TLA_IN_BOUNDS(pair, p.counter_count, a.error)) p.counters[pair] = 0;
       }
     }
     named_barrier_sync(1, 128);  // red / q_s / flags reuse by the next segment
@@ -969,7 +984,9 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
 #pragma unroll
     for (int u = 0; u < kB; ++u) {
       const int ku = k + u * kWarps;
-      const int sl = ku < S ? seg_slot[ku] : -1;
+      int sl = ku < S ? seg_slot[ku] : -1;
+      if (sl >= 0 && !TLA_IN_BOUNDS((static_cast<long long>(sl) + 1) * G * (D + 2) - 1, p.scratch_floats, a.error))
+        sl = -1;
       mk[u] = -INFINITY;
       lk[u] = 0.f;
 #pragma unroll
@@ -1032,6 +1049,7 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
     L += red[1][w] * wt[w];
   }
   const size_t hrow = static_cast<size_t>(b) * a.Hq + kvh * G + r;
+  if (!TLA_IN_BOUNDS(hrow, static_cast<long long>(p.batch) * a.Hq, a.error)) return;
   for (int c = tid; c < kCols; c += NT) {
     float o = 0.f;
 #pragma unroll
@@ -1310,13 +1328,15 @@ DecodeParams decode_params(const tla_layer* L, const void* qkv, const int32_t* p
   p.partial_out = partial;
   p.scratch = L->ctx->d_partials;
   p.counters = L->ctx->d_counters;
+  p.scratch_floats = static_cast<long long>(L->ctx->partial_floats);
+  p.counter_count = static_cast<long long>(L->ctx->counter_count);
   p.batch = batch;
   p.slot_offset = slot_offset;
   p.local_tokens = local_tokens;
   p.append = append;
   // Few, long sequences split each (sequence, kv head) over many CTAs: merge
   // those in a separate, fully parallel kernel instead of in the last CTA.
-  p.defer_merge = L->decode_grid > 4 * batch * L->Hk ? 1 : 0;
+  p.defer_merge = L->decode_grid > TLA_DEFER_MERGE_SEGMENTS * batch * L->Hk ? 1 : 0;
   return p;
 }
 }  // namespace

@@ -127,15 +127,18 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(LayerArgs a, cons
     } else {
       const int kh = h - Hq;
       CT* kc = static_cast<CT*>(a.k_cache);
-      kc[((static_cast<size_t>(b) * Hk + kh) * a.max_tokens + slot) * D + d] = from_f32<CT>(val);
+      const size_t ci = ((static_cast<size_t>(b) * Hk + kh) * a.max_tokens + slot) * D + d;
+      if (TLA_IN_BOUNDS(ci, static_cast<long long>(a.max_batch) * Hk * a.max_tokens * D, a.error))
+        kc[ci] = from_f32<CT>(val);
     }
   }
   if (append) {
     CT* vc = static_cast<CT*>(a.v_cache);
     for (int i = threadIdx.x; i < Hk * D; i += kThreads) {
       const int kh = i / D, d = i - kh * D;
-      vc[((static_cast<size_t>(b) * Hk + kh) * a.max_tokens + slot) * D + d] =
-          from_f32<CT>(x[(Hq + Hk + kh) * D + d]);
+      const size_t ci = ((static_cast<size_t>(b) * Hk + kh) * a.max_tokens + slot) * D + d;
+      if (TLA_IN_BOUNDS(ci, static_cast<long long>(a.max_batch) * Hk * a.max_tokens * D, a.error))
+        vc[ci] = from_f32<CT>(x[(Hq + Hk + kh) * D + d]);
     }
   }
 }
@@ -172,7 +175,7 @@ __global__ void __launch_bounds__(kThreads)
   for (int c = lo; c <= hi; c += kThreads) {
     const int tok = c + threadIdx.x;
     float s = -INFINITY;
-    if (tok <= hi) {
+    if (tok <= hi && TLA_IN_BOUNDS(tok, a.max_tokens, a.error)) {
       const CT* kr = kc + static_cast<size_t>(tok) * D;
       float dot = 0.f;
       for (int d = 0; d < D; ++d) dot += q[d] * to_f32(kr[d]);
@@ -490,7 +493,12 @@ __global__ void __launch_bounds__(128, rope_min_blocks<D>()) rope_rows_kernel(La
         dst = kc + ((static_cast<size_t>(b) * Hk + (hh - Hq)) * a.max_tokens + pos) * D + d0;
       else
         dst = vc + ((static_cast<size_t>(b) * Hk + (hh - Hq - Hk)) * a.max_tokens + pos) * D + d0;
-      *reinterpret_cast<uint4*>(dst) = outv;
+      if (TLA_IN_BOUNDS(hh < Hq ? ((static_cast<long long>(b) * Hq + hh) * seq_len + t) * D + d0 + 7
+                                : ((static_cast<long long>(b) * Hk + (hh - Hq) % Hk) * a.max_tokens + pos) * D + d0 + 7,
+                        hh < Hq ? static_cast<long long>(tokens) * Hq * D
+                                : static_cast<long long>(a.max_batch) * Hk * a.max_tokens * D,
+                        a.error))
+        *reinterpret_cast<uint4*>(dst) = outv;
     }
   }
   griddep_launch_dependents();  // the attention kernel may start its prologue

@@ -516,6 +516,9 @@ __global__ void __launch_bounds__(PCfg<D, DUAL>::kThreads, 1)
       // columns times sigmoid(gate), in fp32 before the conversion to OUT.
       auto gate_cols = [&](float (&o)[32], int c) {
         if (p.gate == nullptr || r >= rows) return;
+        if (!TLA_IN_BOUNDS(base + r * row_stride + 32 * c + 31, static_cast<long long>(p.batch) * p.S * p.Hq * D,
+                           p.error))
+          return;
         float gv[32];
         load_row32(static_cast<const OUT*>(p.gate) + base + r * row_stride + 32 * c, gv);
 #pragma unroll
@@ -561,7 +564,10 @@ __global__ void __launch_bounds__(PCfg<D, DUAL>::kThreads, 1)
 #pragma unroll 1
         for (int it = 0; it < kChunks; ++it, row += kRowsPer, src += kRowsPer * kRowBytes, dst += dst_step) {
           const uint4 v = *reinterpret_cast<const uint4*>(src + ((q ^ (row & 7)) << 4));
-          if (row < rows) *reinterpret_cast<uint4*>(dst) = v;
+          if (row < rows &&
+              TLA_IN_BOUNDS(base + row * row_stride + ((q + 1) * 16) / sizeof(OUT) - 1,
+                            static_cast<long long>(p.batch) * p.S * p.Hq * D, p.error))
+            *reinterpret_cast<uint4*>(dst) = v;
         }
         __syncwarp();  // the stage is reused by the next epilogue
       } else {
@@ -570,7 +576,8 @@ __global__ void __launch_bounds__(PCfg<D, DUAL>::kThreads, 1)
           float o[32];
           tmem_ld32(oe + 32 * c, o);
           gate_cols(o, c);
-          if (r < rows) {
+          if (r < rows && TLA_IN_BOUNDS(base + r * row_stride + 32 * c + 31,
+                                        static_cast<long long>(p.batch) * p.S * p.Hq * D, p.error)) {
             OUT* dst = dst0 + r * row_stride + 32 * c;
             if constexpr (sizeof(OUT) == 2) {
 #pragma unroll

@@ -171,7 +171,9 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
     for (int c = 0; c < p.NT / 32; ++c) {
       float v[32];
       tmem_ld32(lane_base + 32 * c, v);
-      if (!valid) continue;
+      if (!valid || !TLA_IN_BOUNDS(static_cast<long long>(row) * p.N + n0 + 32 * c + 31,
+                                   static_cast<long long>(p.rows) * p.N, p.error))
+        continue;
       float* dst = p.ws + static_cast<size_t>(row) * p.N + n0 + 32 * c;
 #pragma unroll
       for (int i = 0; i < 8; ++i)
@@ -298,7 +300,13 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
           }
           pk[e / 2] = pack_half2(y[0], y[1]);
         }
-        *reinterpret_cast<uint4*>(dst + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        if (TLA_IN_BOUNDS(isq ? (p.mode == kQkvDecode ? (static_cast<long long>(b) * a.Hq + hh + 1) * D
+                                                       : ((static_cast<long long>(b) * a.Hq + hh) * p.S + t + 1) * D) - 1
+                              : ((static_cast<long long>(b) * a.Hk + (hh - a.Hq) % a.Hk) * a.max_tokens + pos + 1) * D - 1,
+                          isq ? static_cast<long long>(p.rows) * a.Hq * D
+                              : static_cast<long long>(a.max_batch) * a.Hk * a.max_tokens * D,
+                          a.error))
+          *reinterpret_cast<uint4*>(dst + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
     }
   } else if (p.mode == kOutPush) {
@@ -324,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
       if (!valid) continue;
       const int col = n0 + 32 * c;
       const size_t o = static_cast<size_t>(row) * p.N + col;
+      if (!TLA_IN_BOUNDS(o + 31, static_cast<long long>(p.rows) * p.N, p.error)) continue;
       if (p.bias) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += __ldg(p.bias + col + i);
@@ -386,15 +395,20 @@ CUresult make_map_2d(const tla_ctx* ctx, const void* base, uint64_t inner, uint6
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-// Widest tile (<= 256 columns, a multiple of `unit` dividing N) that still gives
-// every SM a tile; the narrowest if none does (few rows: decode).
+// Tile width: the widest (<= 256 columns, a multiple of `unit` dividing N)
+// that still gives every SM a tile. With too few tiles even at the narrowest
+// width (few rows: decode), the widest instead: the weights [in][out] are then
+// read as 512-byte row pieces, and split-K supplies the CTAs.
 int choose_nt(int N, int unit, int m_tiles, int sms) {
-  int best = 0;
+  int best = 0, widest = 0, narrowest = 0;
   for (int nt = unit; nt <= 256; nt += unit) {
     if (N % nt) continue;
-    if (best == 0 || static_cast<long long>(m_tiles) * (N / nt) >= sms) best = nt;
+    if (narrowest == 0) narrowest = nt;
+    widest = nt;
+    if (static_cast<long long>(m_tiles) * (N / nt) >= sms) best = nt;
   }
-  return best;
+  if (best) return best;
+  return static_cast<long long>(m_tiles) * (N / narrowest) >= sms ? narrowest : widest;
 }
 
 template <int D>
@@ -404,9 +418,9 @@ cudaError_t launch_proj_t(tla_ctx* ctx, ProjParams& p, cudaStream_t stream) {
   // Few tiles (decode rows): split the reduction dimension so that about two
   // CTAs per SM stream the weights (4 stages each, so two fit on an SM).
   p.ksplit = 1;
-  if (tiles < ctx->sm_count && kc_all >= 8) {
+  if (tiles < ctx->sm_count && kc_all >= 4) {
     int ks = (2 * ctx->sm_count + tiles - 1) / tiles;
-    if (ks > kc_all / 4) ks = kc_all / 4;
+    if (ks > kc_all / 2) ks = kc_all / 2;  // at least two 64-element chunks per CTA
     if (ks > 1) {
       const size_t ws = static_cast<size_t>(p.rows) * p.N;
       if (ensure_proj_workspace(ctx, ws, tiles) == cudaSuccess) {

@@ -29,6 +29,7 @@ LayerArgs layer_args(const tla_layer* L) {
   a.D = L->D;
   a.G = L->G;
   a.max_tokens = L->max_tokens;
+  a.max_batch = L->max_batch;
   a.rotary = L->rotary;
   a.freq_half = L->freq_half;
   a.pair_count = L->pair_count;
@@ -225,6 +226,7 @@ const char* tla_status_string(int status) {
     case TLA_ERR_NO_DEVICE: return "no CUDA device";
     case TLA_ERR_SHARED: return "layer borrows another layer's cache";
     case TLA_ERR_SCRATCH_LIMIT: return "request exceeds the fixed scratch of the allocation-free decode";
+    case TLA_ERR_BOUNDS: return "index outside its buffer (bounds-check build)";
     default: return "unknown status";
   }
 }

@@ -27,6 +27,21 @@ __device__ __forceinline__ void report_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// Bounds-check builds (-DTLA_BOUNDS_CHECK): a guarded global index is checked
+// against its buffer's extent; a bad one records TLA_ERR_BOUNDS and the access
+// is skipped, with control flow and barriers unchanged. Other builds compile
+// the guard to `true`.
+#ifdef TLA_BOUNDS_CHECK
+__device__ __forceinline__ bool in_bounds_checked(long long i, long long n, int* err) {
+  if (i >= 0 && i < n) return true;
+  report_error(err, TLA_ERR_BOUNDS);
+  return false;
+}
+#define TLA_IN_BOUNDS(i, n, err) ::tla::in_bounds_checked(static_cast<long long>(i), static_cast<long long>(n), (err))
+#else
+#define TLA_IN_BOUNDS(i, n, err) true
+#endif
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

@@ -88,7 +88,7 @@ struct LayerArgs {
   const float* k_norm;  // null => none
   int* error;
   int Hq, Hk, D, G;
-  int max_tokens;
+  int max_tokens, max_batch;
   int rotary, freq_half, pair_count, sliding;
   float attn_scale, attn_factor, rms_eps;
   int v_norm, offset_rms;
