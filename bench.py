@@ -1156,7 +1156,8 @@ def main():
     ap.add_argument("--ref-batch", type=int, default=64)
     ap.add_argument("--ref-no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--headline-only", action="store_true", help="skip the sub-records")
+    ap.add_argument("--headline-only", "--no-prefill", dest="headline_only", action="store_true",
+                    help="skip the sub-records")
     ap.add_argument("--min-seconds", type=float, default=1.0, help="timed work of the headline record")
     ap.add_argument("--sub-seconds", type=float, default=0.3, help="timed work of each decode sub-record")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],

@@ -395,20 +395,17 @@ CUresult make_map_2d(const tla_ctx* ctx, const void* base, uint64_t inner, uint6
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-// Tile width: the widest (<= 256 columns, a multiple of `unit` dividing N)
-// that still gives every SM a tile. With too few tiles even at the narrowest
-// width (few rows: decode), the widest instead: the weights [in][out] are then
-// read as 512-byte row pieces, and split-K supplies the CTAs.
+// Widest tile (<= 256 columns, a multiple of `unit` dividing N) that still gives
+// every SM a tile; the narrowest if none does (few rows: decode, where split-K
+// then supplies the CTAs; a wider tile there was measured slower, its split-K
+// sums being larger than the weights it saves reading as wider row pieces).
 int choose_nt(int N, int unit, int m_tiles, int sms) {
-  int best = 0, widest = 0, narrowest = 0;
+  int best = 0;
   for (int nt = unit; nt <= 256; nt += unit) {
     if (N % nt) continue;
-    if (narrowest == 0) narrowest = nt;
-    widest = nt;
-    if (static_cast<long long>(m_tiles) * (N / nt) >= sms) best = nt;
+    if (best == 0 || static_cast<long long>(m_tiles) * (N / nt) >= sms) best = nt;
   }
-  if (best) return best;
-  return static_cast<long long>(m_tiles) * (N / narrowest) >= sms ? narrowest : widest;
+  return best;
 }
 
 template <int D>
