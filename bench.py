@@ -698,7 +698,7 @@ def run_prefill(pkg, torch, device, rank, world, args, tc, src, cpu=True):
     torch.cuda.synchronize()
     steps = args.steps
     est = timed_blocks(torch, pf.call, steps, 1, world, per_call=pf.flush.zero_)[0]
-    repeats = agree_repeats(torch, est, 0.05, world, lo=5, hi=200)
+    repeats = agree_repeats(torch, est, min(0.05, args.sub_seconds), world, lo=5, hi=200)
     times = timed_blocks(torch, pf.call, steps, repeats, world, per_call=pf.flush.zero_)
     st = stats(times, steps)
     err = pf.layer.context.error()
@@ -844,7 +844,7 @@ def run_qkv_prefill(pkg, torch, device, rank, world, args, tc):
         call()
     torch.cuda.synchronize()
     est = timed_blocks(torch, call, args.steps, 1, world, per_call=flush.zero_)[0]
-    repeats = agree_repeats(torch, est, 0.05, world, lo=5, hi=200)
+    repeats = agree_repeats(torch, est, min(0.05, args.sub_seconds), world, lo=5, hi=200)
     st = stats(timed_blocks(torch, call, args.steps, repeats, world, per_call=flush.zero_), args.steps)
     if layer.context.error() != 0:
         raise RuntimeError("device reported an error")
@@ -934,8 +934,8 @@ def run_out_proj(pkg, torch, device, rank, world, args, hbm):
         graph.replay()
         torch.cuda.synchronize()
         est = timed_blocks(torch, graph.replay, args.steps, 1, world)[0]
-        out = stats(timed_blocks(torch, graph.replay, args.steps, agree_repeats(torch, est, 0.2, world), world),
-                    args.steps)
+        out = stats(timed_blocks(torch, graph.replay, args.steps, agree_repeats(torch, est, args.sub_seconds, world),
+                                 world), args.steps)
         del graph  # may hold NCCL work: released before the process group goes away
         torch.cuda.synchronize()
         return out
@@ -1150,7 +1150,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode_1b",
-                    choices=["decode_1b", "ragged_8b", "long_ctx", "long_ctx_heads", "prefill_05b"],
+                    choices=["decode_1b", "ragged_8b", "long_ctx", "long_ctx_heads", "prefill_05b", "out_proj",
+                             "prefill_qkv"],
                     help="headline workload (long_ctx: token blocks; the default line carries all as sub-records)")
     ap.add_argument("--batch", type=int, default=DECODE_1B["batch"], help="decode_1b sequences per GPU")
     ap.add_argument("--ref-batch", type=int, default=64)
@@ -1183,6 +1184,15 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
     hbm, tc, src = peaks()
     single = {"ragged_8b": Ragged8B, "long_ctx": LongCtxSeq, "long_ctx_heads": LongCtxHeads}
+    if args.workload in ("out_proj", "prefill_qkv"):  # one sub-record alone (profiling)
+        rec = (run_out_proj(pkg, torch, device, rank, world, args, hbm) if args.workload == "out_proj"
+               else run_qkv_prefill(pkg, torch, device, rank, world, args, tc))
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "workload": args.workload, args.workload: rec}), flush=True)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return
     if args.workload == "prefill_05b":
         rec = run_prefill(pkg, torch, device, rank, world, args, tc, src)
         if rank == 0:
