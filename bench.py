@@ -773,6 +773,16 @@ class QkvDecode1B(Decode1B):
             if rc:
                 raise RuntimeError(f"tla_qkv_decode: {rc}")
 
+    def e2e_setup(self):
+        super().e2e_setup()
+        self.h2d = self.x.numel() * 2 + self.pos.numel() * 4
+        self.x_host = self.x.cpu().pin_memory()
+
+    def e2e_step(self):
+        self.x.copy_(self.x_host, non_blocking=True)
+        self.step()
+        self.out_host.copy_(self.outs, non_blocking=True)
+
     def parity(self, world, rank):
         from oracle import oracle
 
@@ -1151,7 +1161,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode_1b",
                     choices=["decode_1b", "ragged_8b", "long_ctx", "long_ctx_heads", "prefill_05b", "out_proj",
-                             "prefill_qkv"],
+                             "prefill_qkv", "qkv_decode_1b"],
                     help="headline workload (long_ctx: token blocks; the default line carries all as sub-records)")
     ap.add_argument("--batch", type=int, default=DECODE_1B["batch"], help="decode_1b sequences per GPU")
     ap.add_argument("--ref-batch", type=int, default=64)
@@ -1183,7 +1193,8 @@ def main():
     if world > 1:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
     hbm, tc, src = peaks()
-    single = {"ragged_8b": Ragged8B, "long_ctx": LongCtxSeq, "long_ctx_heads": LongCtxHeads}
+    single = {"ragged_8b": Ragged8B, "long_ctx": LongCtxSeq, "long_ctx_heads": LongCtxHeads,
+              "qkv_decode_1b": QkvDecode1B}
     if args.workload in ("out_proj", "prefill_qkv"):  # one sub-record alone (profiling)
         rec = (run_out_proj(pkg, torch, device, rank, world, args, hbm) if args.workload == "out_proj"
                else run_qkv_prefill(pkg, torch, device, rank, world, args, tc))

@@ -31,7 +31,7 @@ namespace tla {
 
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;  // warps 0-3: TMA / MMA, then epilogue; all 8 warps run the epilogue
 constexpr int kXStage = 128 * 128;  // x: 128 rows x 64 fp16 (one 128-byte row each)
 constexpr int kWBox = 64 * 128;     // W: 64 rows of the reduction dim x 64 fp16 columns
 enum : int { kQkvDecode = 0, kQkvPrefill = 1, kOutProj = 2, kOutPush = 3 };
@@ -70,7 +70,7 @@ __host__ __device__ inline int stage_bytes(int NT) { return kXStage + (NT / 64) 
 
 template <int D>
 __host__ __device__ inline int epilogue_bytes(int mode) {
-  return mode >= kOutProj ? 0 : 2 * kThreads * (D + 1) * 4;  // each row's head values and its cos / sin
+  return mode >= kOutProj ? 0 : 3 * 128 * (D + 1) * 4;  // each row's cos / sin, and its head values per warp set
 }
 
 template <int D>
@@ -162,13 +162,15 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
   __syncwarp();
   tc_fence_after();
 
-  const int r = tid, row = m0 + r;
+  // Epilogue: thread = row (TMEM lane) in each of two warp sets (warps 0-3 and
+  // 4-7 read the same lanes), which take alternate 32-column chunks or heads.
+  const int set = warp >> 2, r = tid & 127, row = m0 + r;
   const bool valid = row < p.rows;
-  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
   if (p.ksplit > 1) {
     // add this CTA's partial tile into the workspace; the last CTA of the tile
     // goes on to the epilogue, reading the complete sums from the workspace
-    for (int c = 0; c < p.NT / 32; ++c) {
+    for (int c = set; c < p.NT / 32; c += 2) {
       float v[32];
       tmem_ld32(lane_base + 32 * c, v);
       if (!valid || !TLA_IN_BOUNDS(static_cast<long long>(row) * p.N + n0 + 32 * c + 31,
@@ -233,19 +235,21 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
       }
     }
     const bool ok = valid && pos >= 0 && pos < a.max_tokens;
-    if (valid && !ok && n0 == 0) report_error(a.error, TLA_ERR_POSITION);  // the row is skipped
-    float* hrow = reinterpret_cast<float*>(smem) + r * (D + 1);                   // padded: no bank conflicts
-    float* cs = reinterpret_cast<float*>(smem) + kThreads * (D + 1) + r * (D + 1);  // cos [half], sin [half]
+    if (valid && !ok && n0 == 0 && set == 0) report_error(a.error, TLA_ERR_POSITION);  // the row is skipped
+    float* cs = reinterpret_cast<float*>(smem) + r * (D + 1);                          // cos [half], sin [half]
+    float* hrow = reinterpret_cast<float*>(smem) + (1 + set) * 128 * (D + 1) + r * (D + 1);  // padded rows
     const int half = a.rotary / 2;
     const int head0 = n0 / D, heads = p.NT / D;
-    if (ok && half > 0 && head0 < a.Hq + a.Hk)  // the tile holds a Q or K head: this row's RoPE factors
+    if (set == 0 && ok && half > 0 && head0 < a.Hq + a.Hk)  // the tile holds a Q or K head: this row's RoPE factors
       for (int i = 0; i < half; ++i) {
         float c = 1.f, s = 0.f;
         if (i < a.pair_count) rope_cos_sin(pos, __ldg(a.inv_freq + i), &c, &s);
         cs[i] = c;
         cs[half + i] = s;
       }
-    for (int j = 0; j < heads; ++j) {
+    __syncthreads();
+    const bool full_rope = a.rotary == D && a.pair_count == D / 2;
+    for (int j = set; j < heads; j += 2) {
       const int hh = head0 + j;
       float ss = 0.f;
 #pragma unroll
@@ -270,16 +274,43 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
         return x;
       };
       __half* dst;
-      if (isq)
-        dst = p.qout + (p.mode == kQkvDecode ? (static_cast<size_t>(b) * a.Hq + hh) * D
-                                             : ((static_cast<size_t>(b) * a.Hq + hh) * p.S + t) * D);
-      else if (isk)
-        dst = static_cast<__half*>(a.k_cache) +
-              ((static_cast<size_t>(b) * a.Hk + (hh - a.Hq)) * a.max_tokens + pos) * D;
-      else
-        dst = static_cast<__half*>(a.v_cache) +
-              ((static_cast<size_t>(b) * a.Hk + (hh - a.Hq - a.Hk)) * a.max_tokens + pos) * D;
+      long long di, dn;  // element offset of dst and the buffer's extent (bounds-check builds)
+      if (isq) {
+        di = p.mode == kQkvDecode ? (static_cast<long long>(b) * a.Hq + hh) * D
+                                  : ((static_cast<long long>(b) * a.Hq + hh) * p.S + t) * D;
+        dn = static_cast<long long>(p.rows) * a.Hq * D;
+        dst = p.qout + di;
+      } else {
+        di = ((static_cast<long long>(b) * a.Hk + (hh - a.Hq) % a.Hk) * a.max_tokens + pos) * D;
+        dn = static_cast<long long>(a.max_batch) * a.Hk * a.max_tokens * D;
+        dst = static_cast<__half*>(isk ? a.k_cache : a.v_cache) + di;
+      }
+      if (!TLA_IN_BOUNDS(di + D - 1, dn, a.error)) continue;
       const bool rope = (isq || isk) && half > 0;
+      if (rope && full_rope) {
+        // rotate-half RoPE over the whole head (math.ts:134-147), dims i and
+        // i + D/2 together, branch-free
+#pragma unroll
+        for (int i0 = 0; i0 < D / 2; i0 += 8) {
+          uint32_t lo[4], hi[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            float l2[2], h2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int i = i0 + e + u;
+              const float x = val(i), y = val(i + D / 2), c = cs[i], sn = cs[D / 2 + i];
+              l2[u] = (x * c - y * sn) * a.attn_factor;
+              h2[u] = (y * c + x * sn) * a.attn_factor;
+            }
+            lo[e / 2] = pack_half2(l2[0], l2[1]);
+            hi[e / 2] = pack_half2(h2[0], h2[1]);
+          }
+          *reinterpret_cast<uint4*>(dst + i0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<uint4*>(dst + D / 2 + i0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        }
+        continue;
+      }
       for (int d0 = 0; d0 < D; d0 += 8) {
         uint32_t pk[4];
 #pragma unroll
@@ -289,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
           for (int u = 0; u < 2; ++u) {
             const int d = d0 + e + u;
             float x = val(d);
-            if (rope && d < a.rotary) {  // rotate-half RoPE, math.ts:134-147
+            if (rope && d < a.rotary) {  // rotate-half RoPE, math.ts:134-147 (partial rotary / pair count)
               const int jj = d < half ? d : d - half;
               if (jj < a.pair_count) {
                 const float partner = d < half ? -val(d + half) : val(d - half);
@@ -300,13 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
           }
           pk[e / 2] = pack_half2(y[0], y[1]);
         }
-        if (TLA_IN_BOUNDS(isq ? (p.mode == kQkvDecode ? (static_cast<long long>(b) * a.Hq + hh + 1) * D
-                                                       : ((static_cast<long long>(b) * a.Hq + hh) * p.S + t + 1) * D) - 1
-                              : ((static_cast<long long>(b) * a.Hk + (hh - a.Hq) % a.Hk) * a.max_tokens + pos + 1) * D - 1,
-                          isq ? static_cast<long long>(p.rows) * a.Hq * D
-                              : static_cast<long long>(a.max_batch) * a.Hk * a.max_tokens * D,
-                          a.error))
-          *reinterpret_cast<uint4*>(dst + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(dst + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
     }
   } else if (p.mode == kOutPush) {
@@ -315,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
     uint8_t* dst = p.x.peers[owner] + static_cast<size_t>(epoch & 1u) * p.x.region_bytes;
     const size_t word0 = static_cast<size_t>(p.x.rank) * p.x.slot_words + static_cast<size_t>(row) * p.cols +
                          (n0 - owner * p.cols);
-    for (int c = 0; c < p.NT / 32; ++c) {
+    for (int c = set; c < p.NT / 32; c += 2) {
       float v[32];
       load_acc(32 * c, v);
       if (!valid) continue;
@@ -326,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
     }
   } else {
     // ---------------------------------------------------------------- output projection epilogue
-    for (int c = 0; c < p.NT / 32; ++c) {
+    for (int c = set; c < p.NT / 32; c += 2) {
       float v[32];
       load_acc(32 * c, v);
       if (!valid) continue;
@@ -416,7 +441,7 @@ cudaError_t launch_proj_t(tla_ctx* ctx, ProjParams& p, cudaStream_t stream) {
   // CTAs per SM stream the weights (4 stages each, so two fit on an SM).
   p.ksplit = 1;
   if (tiles < ctx->sm_count && kc_all >= 4) {
-    int ks = (2 * ctx->sm_count + tiles - 1) / tiles;
+    int ks = (2 * ctx->sm_count) / tiles;  // one resident wave at two CTAs per SM
     if (ks > kc_all / 2) ks = kc_all / 2;  // at least two 64-element chunks per CTA
     if (ks > 1) {
       const size_t ws = static_cast<size_t>(p.rows) * p.N;
