@@ -766,12 +766,16 @@ class QkvDecode1B(Decode1B):
 
         s = ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
         for i, layer in enumerate(self.layers):
+            if record:
+                record[0]()
             rc = self.lib.tla_qkv_decode(layer.handle, ctypes.c_void_p(self.x[i].data_ptr()),
                                          ctypes.c_void_p(self.w[i].data_ptr()), ctypes.c_void_p(self.b[i].data_ptr()),
                                          HIDDEN_1B, ctypes.c_void_p(self.pos.data_ptr()), None,
                                          ctypes.c_void_p(self.outs[i].data_ptr()), self.x.shape[1], s)
             if rc:
                 raise RuntimeError(f"tla_qkv_decode: {rc}")
+            if record:
+                record[1]()
 
     def e2e_setup(self):
         super().e2e_setup()
