@@ -14,43 +14,13 @@
 // stops waiting, runs its remaining control flow and frees its TMEM.
 #include <math.h>
 
-#include "tcgen05.cuh"
-#include "tla_device.cuh"
-#include "tla_internal.h"
+#include "prefill_common.cuh"
 
 namespace tla {
 
 namespace {
 
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescaleLog2 = 8.f;  // a row's reference maximum moves only when exceeded by 2^8
-
-struct PrefillParams {
-  CUtensorMap tm_q;  // rotated queries [B*Hq][S][D] fp16, 128-row boxes
-  CUtensorMap tm_k;  // cache [max_batch*Hk][max_tokens][D] fp16, 128-token boxes
-  CUtensorMap tm_v;
-  void* out;
-  const void* gate;  // null, or [B][S][Hq][D] like out: out *= sigmoid(gate)
-  const int32_t* start;
-  int* error;
-  int S, Hq, Hk, G, sliding, batch, num_m;
-  float scale_log2;
-};
-
-// 2^x on the FMA pipe, for part of the softmax exponentials (the MUFU unit is the
-// bottleneck at head_dim 64). Cody-Waite split x = j + f with j = rint(x) (the
-// 1.5 * 2^23 rounding trick, j ends up in the low mantissa bits), f in [-0.5, 0.5];
-// 2^f from a cubic least-squares fit on Chebyshev nodes of [-0.5, 0.5]
-// (max relative error 7.7e-5, below fp16 resolution); 2^j is added to the
-// exponent field. Inputs below -126 (masked scores) give a subnormal that
-// rounds to 0 in fp16.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.05508868f, f, 0.24260405f), f, 0.69327623f), f, 0.99992895f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
+using namespace prefill;
 
 #ifdef TLA_PREFILL_TRACE
 // Optional pipeline trace (builds with -DTLA_PREFILL_TRACE only): SM clock of
@@ -70,90 +40,13 @@ __device__ unsigned long long g_prefill_trace[64][16];
   } while (0)
 #endif
 
+#ifndef TLA_PREFILL_PP
+#define TLA_PREFILL_PP 1  // head_dim 64: the two-tile kernel of prefill_pp.cu (0: prefill_tc_kernel)
+#endif
+
 #ifndef TLA_PREFILL_DUAL
 #define TLA_PREFILL_DUAL 0  // head_dim 64: two pipelines per CTA (measured slower; 0: one)
 #endif
-
-#ifndef TLA_PREFILL_POLY_EVERY
-#define TLA_PREFILL_POLY_EVERY 0  // every n-th pair of exponentials goes to the FMA pipe (0: none)
-#endif
-
-// Whether pair `i` of a row's exponentials is evaluated with ex2_poly.
-__device__ __forceinline__ constexpr bool poly_pair(int i) {
-#if TLA_PREFILL_POLY_EVERY > 0
-  return i % TLA_PREFILL_POLY_EVERY == TLA_PREFILL_POLY_EVERY - 1;
-#else
-  return i < 0;
-#endif
-}
-
-// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two
-// columns' FMA or add, each element rounded as its scalar counterpart).
-__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-// (a0, a1) * b2 + c2
-__device__ __forceinline__ void fma_f32x2(float a0, float a1, uint64_t b2, uint64_t c2, float& r0, float& r1) {
-  asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%2, %3};\n\tfma.rn.f32x2 d, a, %4, %5;\n\tmov.b64 {%0, %1}, d;\n\t}"
-      : "=f"(r0), "=f"(r1)
-      : "f"(a0), "f"(a1), "l"(b2), "l"(c2));
-}
-// acc += (e0, e1)
-__device__ __forceinline__ void add_f32x2(uint64_t& acc, float e0, float e1) {
-  asm("{\n\t.reg .b64 e;\n\tmov.b64 e, {%1, %2};\n\tadd.rn.f32x2 %0, %0, e;\n\t}" : "+l"(acc) : "f"(e0), "f"(e1));
-}
-__device__ __forceinline__ float sum_f32x2(uint64_t v) {
-  float lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-  return lo + hi;
-}
-
-// 64 consecutive fp32 columns of this thread's TMEM lane (two loads, one wait).
-__device__ __forceinline__ void tmem_ld64x(uint32_t taddr, uint32_t (&r)[64]) {
-#pragma unroll
-  for (int k = 0; k < 2; ++k)
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[k * 32 + 0]), "=r"(r[k * 32 + 1]), "=r"(r[k * 32 + 2]), "=r"(r[k * 32 + 3]), "=r"(r[k * 32 + 4]),
-          "=r"(r[k * 32 + 5]), "=r"(r[k * 32 + 6]), "=r"(r[k * 32 + 7]), "=r"(r[k * 32 + 8]), "=r"(r[k * 32 + 9]),
-          "=r"(r[k * 32 + 10]), "=r"(r[k * 32 + 11]), "=r"(r[k * 32 + 12]), "=r"(r[k * 32 + 13]),
-          "=r"(r[k * 32 + 14]), "=r"(r[k * 32 + 15]), "=r"(r[k * 32 + 16]), "=r"(r[k * 32 + 17]),
-          "=r"(r[k * 32 + 18]), "=r"(r[k * 32 + 19]), "=r"(r[k * 32 + 20]), "=r"(r[k * 32 + 21]),
-          "=r"(r[k * 32 + 22]), "=r"(r[k * 32 + 23]), "=r"(r[k * 32 + 24]), "=r"(r[k * 32 + 25]),
-          "=r"(r[k * 32 + 26]), "=r"(r[k * 32 + 27]), "=r"(r[k * 32 + 28]), "=r"(r[k * 32 + 29]),
-          "=r"(r[k * 32 + 30]), "=r"(r[k * 32 + 31])
-        : "r"(taddr + k * 32));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// 32 consecutive values of a gate row, as floats (16-byte loads).
-template <typename T>
-__device__ __forceinline__ void load_row32(const T* src, float (&v)[32]) {
-  if constexpr (sizeof(T) == 2) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 u = *reinterpret_cast<const uint4*>(src + 8 * i);
-      const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        v[8 * i + 2 * k] = __low2float(h[k]);
-        v[8 * i + 2 * k + 1] = __high2float(h[k]);
-      }
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 f = *reinterpret_cast<const float4*>(src + 4 * i);
-      v[4 * i] = f.x;
-      v[4 * i + 1] = f.y;
-      v[4 * i + 2] = f.z;
-      v[4 * i + 3] = f.w;
-    }
-  }
-}
 
 // ---------------------------------------------------------------- the kernel
 // Persistent: one CTA per SM walks a fixed list of work items, an item being
@@ -259,12 +152,6 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
   return w;
 }
 
-// Item index of this CTA's k-th item (snake order over the grid), or -1.
-__device__ __forceinline__ int prefill_item_of(int k, int num_items) {
-  const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
-  const int it = k * G + ((k & 1) ? G - 1 - c : c);
-  return it < num_items ? it : -1;
-}
 
 template <int D, typename OUT, bool DUAL>
 __global__ void __launch_bounds__(PCfg<D, DUAL>::kThreads, 1)
@@ -791,17 +678,6 @@ __global__ void __launch_bounds__(PCfg<D, DUAL>::kThreads, 1)
   }
 }
 
-CUresult make_map(const tla_layer* L, void* base, uint64_t rows, uint64_t planes, CUtensorMap* map,
-                  uint32_t box_rows = 128) {
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(L->D), rows, planes};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(L->D) * 2, static_cast<cuuint64_t>(L->D) * 2 * rows};
-  const cuuint32_t box[3] = {64, box_rows, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return L->ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-}
-
 template <int D, typename OUT, bool DUAL>
 cudaError_t set_smem() {
   return raise_smem_limit(reinterpret_cast<const void*>(prefill_tc_kernel<D, OUT, DUAL>), PCfg<D, DUAL>::kSmem);
@@ -823,7 +699,10 @@ cudaError_t prefill_fast_configure(tla_layer* L) {
       make_map(L, L->v_cache, L->max_tokens, planes, &L->tmap_v128) != CUDA_SUCCESS)
     return cudaSuccess;
   cudaError_t e;
-  if (L->D == 64) {  // two pipelines per CTA
+  if (L->D == 64 && TLA_PREFILL_PP) {  // two query tiles per CTA
+    e = pp_configure(L);
+    L->prefill_smem = pp_smem();
+  } else if (L->D == 64) {
     constexpr bool kDual = TLA_PREFILL_DUAL != 0;
     e = L->io_fp32 ? set_smem<64, float, kDual>() : set_smem<64, __half, kDual>();
     L->prefill_smem = PCfg<64, kDual>::kSmem;
@@ -864,6 +743,7 @@ cudaError_t launch_prefill_attention(const tla_layer* L, const int32_t* start, c
   p.batch = batch;
   p.scale_log2 = L->attn_scale * kLog2e;
   p.num_m = (seq_len + 127) / 128;
+  if (L->D == 64 && TLA_PREFILL_PP) return launch_pp(L, p, stream);
   const int items = p.num_m * batch * L->Hq;
   const dim3 grid(static_cast<unsigned>(items < L->ctx->sm_count ? items : L->ctx->sm_count));
   if (L->D == 64) {
