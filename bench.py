@@ -719,7 +719,7 @@ def run_prefill(pkg, torch, device, rank, world, args, tc, src, cpu=True):
            "tflops": round(tflops, 2), "ms": round(ms, 5), "ms_p10": round(st["p10"], 5),
            "ms_p90": round(st["p90"], 5), "calls": st["blocks"] * steps, "causal_gflop": round(pf.flops / 1e9, 3),
            "frac": round(tflops / world / tc, 4), "peak_tflops": tc, "peak_source": src,
-           "kernels": "rope_rows_kernel<64> + prefill_tc_kernel<64,half> (persistent)",
+           "kernels": "rope_rows_kernel<64> + prefill_pp_kernel<half> (persistent, two query tiles per CTA)",
            "gpu_launches": int(2 * st["blocks"] * steps), "scaling": "strong",
            "e2e": {"tflops": round(pf.flops / (e2e_ms * 1e-3) / 1e12, 2), "ms": round(e2e_ms, 5),
                    "h2d_bytes_per_call": pf.h2d, "d2h_bytes_per_call": pf.d2h,
@@ -870,7 +870,7 @@ def run_qkv_prefill(pkg, torch, device, rank, world, args, tc):
            "tflops": round(flops / (ms * 1e-3) / 1e12, 2), "ms": round(ms, 5), "ms_p10": round(st["p10"], 5),
            "ms_p90": round(st["p90"], 5), "gflop": round(flops / 1e9, 3),
            "frac": round(flops / (ms * 1e-3) / 1e12 / world / tc, 4),
-           "kernels": "proj_tc_kernel<64> (QKV + RoPE/append epilogue) + prefill_tc_kernel<64,half>",
+           "kernels": "proj_tc_kernel<64> (QKV + RoPE/append epilogue) + prefill_pp_kernel<half>",
            "gpu_launches": int(2 * st["blocks"] * args.steps)}
     if rank == 0:  # first 256 positions of the rank's first sequence, first kv head's query group
         from oracle import oracle
