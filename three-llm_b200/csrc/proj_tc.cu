@@ -66,6 +66,23 @@ struct ProjParams {
   int* tile_cnt;  // [m_tiles * (N / NT)], zero between launches
 };
 
+#ifdef TLA_PROJ_TRACE
+// Optional per-CTA timeline (builds with -DTLA_PROJ_TRACE only): globaltimer at
+// [cta][0] entry, [1] after the dependency wait, [2] accumulator complete,
+// [3] split-K partial added and ticket taken, [4] epilogue tables ready,
+// [5] exit of a CTA that ran the epilogue, [6] QKV: a head's values loaded,
+// [7] its rotated rows stored; read with tla_debug_proj_trace.
+__device__ unsigned long long g_proj_trace[1024][8];
+#define PRTRACE(ev)                                                                       \
+  do {                                                                                    \
+    if (threadIdx.x == 0 && blockIdx.x < 1024) g_proj_trace[blockIdx.x][(ev)] = globaltimer(); \
+  } while (0)
+#else
+#define PRTRACE(ev) \
+  do {              \
+  } while (0)
+#endif
+
 __host__ __device__ inline int stage_bytes(int NT) { return kXStage + (NT / 64) * kWBox; }
 
 template <int D>
@@ -73,13 +90,21 @@ __host__ __device__ inline int epilogue_bytes(int mode) {
   return mode >= kOutProj ? 0 : 3 * 128 * (D + 1) * 4;  // each row's cos / sin, and its head values per warp set
 }
 
+// Bytes below the barriers: the stage ring, and the epilogue's tables and
+// rows, which reuse it.
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_constant__ ProjParams p) {
+__host__ __device__ inline int region_bytes(int ring, int mode) {
+  const int epi = epilogue_bytes<D>(mode);
+  return ring > epi ? ring : epi;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 2) proj_tc_kernel(const __grid_constant__ ProjParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int sb = stage_bytes(p.NT);
-  const int ring = p.stages * sb, epi = epilogue_bytes<D>(p.mode);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (ring > epi ? ring : epi));
+  const int ring = p.stages * sb;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + region_bytes<D>(ring, p.mode));
   uint64_t* empty = full + p.stages;
   uint64_t* accb = empty + p.stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
@@ -93,6 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
   const int kc_all = (p.K + 63) / 64;
   const int kc0 = (ks * kc_all) / p.ksplit, kc1 = ((ks + 1) * kc_all) / p.ksplit;
   const int kchunks = kc1 - kc0;  // this CTA's 64-element chunks of the reduction dim
+  PRTRACE(0);
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
@@ -113,11 +139,48 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   griddep_wait();  // x, positions and the residual may come from the previous kernel
+  PRTRACE(1);
   __shared__ int epoch_s;
   const unsigned epoch = p.mode == kOutPush ? xch_epoch(p.x, &epoch_s) : 0u;  // (block-uniform branch)
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     if (*abort_flag) return;
     if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
+  };
+  // QKV modes: this thread's tile row position (threads 0-127, one row each;
+  // -1: no row, or a position outside the cache), loaded now so that its
+  // latency overlaps the mainloop.
+  __shared__ int row_pos[128];
+  int my_pos = -1;
+  if ((p.mode == kQkvDecode || p.mode == kQkvPrefill) && tid < 128 && m0 + tid < p.rows) {
+    const int grow = m0 + tid;
+    if (p.mode == kQkvDecode) {
+      my_pos = p.pos[grow];
+    } else {
+      const int bb = grow / p.S;
+      my_pos = p.pos[bb] + (grow - bb * p.S);
+    }
+    if (my_pos < 0 || my_pos >= p.a.max_tokens) my_pos = -1;
+  }
+  // The rows' positions into row_pos and, for a tile of Q or K heads, their
+  // RoPE factors at tbl + r (D + 1): cos [half], sin [half]. Each factor is
+  // one dependent chain, so all threads share them.
+  auto fill_rope = [&](float* tbl) {
+    const LayerArgs& a = p.a;
+    if (tid < 128) row_pos[tid] = my_pos;
+    __syncthreads();
+    const int half = a.rotary / 2;
+    if (half == 0 || n0 / D >= a.Hq + a.Hk) return;  // V heads: no RoPE
+    for (int e = tid; e < 128 * half; e += kThreads) {  // entry (row rr, pair i) at index rr half + i
+      const int rr = e / half, i = e - rr * half;
+      if (m0 + rr >= p.rows) break;  // rows only grow with e
+      const int ps = row_pos[rr];
+      if (ps < 0) continue;
+      float c = 1.f, sn = 0.f;
+      if (i < a.pair_count) rope_cos_sin(ps, __ldg(a.inv_freq + i), &c, &sn);
+      float* cr = tbl + rr * (D + 1);
+      cr[i] = c;
+      cr[half + i] = sn;
+    }
   };
 
   if (warp == 0 && lane == 0) {
@@ -161,6 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
   wait(accb, 0);
   __syncwarp();
   tc_fence_after();
+  PRTRACE(2);
 
   // Epilogue: thread = row (TMEM lane) in each of two warp sets (warps 0-3 and
   // 4-7 read the same lanes), which take alternate 32-column chunks or heads.
@@ -188,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
     if (tid == 0) epoch_s = atomicAdd(p.tile_cnt + tile, 1) == p.ksplit - 1 ? 1 : 0;
     __syncthreads();
     const bool last = epoch_s != 0;
+    PRTRACE(3);
     __syncthreads();  // epoch_s is reused by the push epilogue
     if (!last) {
       tc_fence_before();
@@ -202,13 +267,12 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
     if (tid == 0) p.tile_cnt[tile] = 0;
   }
   // The tile's accumulator columns [c0, c0 + 32) of this thread's row: from
-  // TMEM (warp-collective), or, split-K, from the workspace, which is zeroed
-  // behind the read for the next launch.
+  // TMEM (warp-collective), or, split-K, from the workspace.
   auto load_acc = [&](int c0, float (&v)[32]) {
     if (p.ksplit == 1) {
       tmem_ld32(lane_base + c0, v);
     } else if (valid) {
-      float4* src = reinterpret_cast<float4*>(p.ws + static_cast<size_t>(row) * p.N + n0 + c0);
+      const float4* src = reinterpret_cast<const float4*>(p.ws + static_cast<size_t>(row) * p.N + n0 + c0);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 q = __ldcg(src + i);
@@ -216,53 +280,82 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
         v[4 * i + 1] = q.y;
         v[4 * i + 2] = q.z;
         v[4 * i + 3] = q.w;
-        __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
       }
+    }
+  };
+  // Split-K: zero the workspace columns [c0, c0 + 32) of this thread's row
+  // for the next launch once they have been read (kept apart from the loads,
+  // so that no store waits behind a load of the same address).
+  auto clear_acc = [&](int c0) {
+    if (p.ksplit == 1 || !valid) return;
+    float4* dst = reinterpret_cast<float4*>(p.ws + static_cast<size_t>(row) * p.N + n0 + c0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) __stcg(dst + i, make_float4(0.f, 0.f, 0.f, 0.f));
+  };
+  // bias columns [c0, c0 + 32) of the tile (zeros without a bias)
+  const bool bias_v4 = (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
+  auto load_bias = [&](int c0, float (&bv)[32]) {
+    if (p.bias == nullptr) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) bv[i] = 0.f;
+    } else if (bias_v4) {
+      const float4* src = reinterpret_cast<const float4*>(p.bias + n0 + c0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 q = __ldg(src + i);
+        bv[4 * i] = q.x;
+        bv[4 * i + 1] = q.y;
+        bv[4 * i + 2] = q.z;
+        bv[4 * i + 3] = q.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) bv[i] = __ldg(p.bias + n0 + c0 + i);
     }
   };
   if (p.mode == kQkvDecode || p.mode == kQkvPrefill) {
     // ---------------------------------------------------------------- QKV epilogue
     const LayerArgs& a = p.a;
-    int b = 0, t = 0, pos = -1;
+    constexpr int kRow = D + 1;  // padded row of the tables (floats)
+    float* const tbl = reinterpret_cast<float*>(smem);  // over the stage ring
+    fill_rope(tbl);
+    __syncthreads();
+    PRTRACE(4);
+    int b = 0, t = 0;
+    const int pos = row_pos[r];
     if (valid) {
       if (p.mode == kQkvDecode) {
         b = row;
-        pos = p.pos[row];
       } else {
         b = row / p.S;
         t = row - b * p.S;
-        pos = p.pos[b] + t;
       }
     }
-    const bool ok = valid && pos >= 0 && pos < a.max_tokens;
+    const bool ok = valid && pos >= 0;
     if (valid && !ok && n0 == 0 && set == 0) report_error(a.error, TLA_ERR_POSITION);  // the row is skipped
-    float* cs = reinterpret_cast<float*>(smem) + r * (D + 1);                          // cos [half], sin [half]
-    float* hrow = reinterpret_cast<float*>(smem) + (1 + set) * 128 * (D + 1) + r * (D + 1);  // padded rows
+    float* cs = tbl + r * kRow;  // cos [half], sin [half]
+    float* hrow = reinterpret_cast<float*>(smem) + (1 + set) * 128 * kRow + r * kRow;  // padded rows
     const int half = a.rotary / 2;
     const int head0 = n0 / D, heads = p.NT / D;
-    if (set == 0 && ok && half > 0 && head0 < a.Hq + a.Hk)  // the tile holds a Q or K head: this row's RoPE factors
-      for (int i = 0; i < half; ++i) {
-        float c = 1.f, s = 0.f;
-        if (i < a.pair_count) rope_cos_sin(pos, __ldg(a.inv_freq + i), &c, &s);
-        cs[i] = c;
-        cs[half + i] = s;
-      }
-    __syncthreads();
     const bool full_rope = a.rotary == D && a.pair_count == D / 2;
     for (int j = set; j < heads; j += 2) {
       const int hh = head0 + j;
       float ss = 0.f;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
-        float v[32];
+        float v[32], bv[32];
         load_acc(j * D + 32 * c, v);  // TMEM: warp-collective, every lane loads
+        load_bias(j * D + 32 * c, bv);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float x = v[i] + (p.bias ? __ldg(p.bias + hh * D + 32 * c + i) : 0.f);
+          const float x = v[i] + bv[i];
           hrow[32 * c + i] = x;
           ss += x * x;
         }
       }
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) clear_acc(j * D + 32 * c);
+      PRTRACE(6);
       if (!ok) continue;
       const bool isq = hh < a.Hq, isk = !isq && hh < a.Hq + a.Hk;
       const float* w = isq ? a.q_norm : (isk ? a.k_norm : nullptr);
@@ -309,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
           *reinterpret_cast<uint4*>(dst + i0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
           *reinterpret_cast<uint4*>(dst + D / 2 + i0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         }
+        PRTRACE(7);
         continue;
       }
       for (int d0 = 0; d0 < D; d0 += 8) {
@@ -348,20 +442,20 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
       for (int i = 0; i < 16; ++i)
         xch_st_v4(dst + (word0 + 32 * c + 2 * i) * 8,
                   make_uint4(__float_as_uint(v[2 * i]), epoch, __float_as_uint(v[2 * i + 1]), epoch));
+      clear_acc(32 * c);
     }
   } else {
     // ---------------------------------------------------------------- output projection epilogue
     for (int c = set; c < p.NT / 32; c += 2) {
-      float v[32];
+      float v[32], bv[32];
       load_acc(32 * c, v);
+      load_bias(32 * c, bv);
       if (!valid) continue;
       const int col = n0 + 32 * c;
       const size_t o = static_cast<size_t>(row) * p.N + col;
       if (!TLA_IN_BOUNDS(o + 31, static_cast<long long>(p.rows) * p.N, p.error)) continue;
-      if (p.bias) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += __ldg(p.bias + col + i);
-      }
+      for (int i = 0; i < 32; ++i) v[i] += bv[i];
       if (p.residual) {
         if (p.res_f32) {
           const float4* res = reinterpret_cast<const float4*>(static_cast<const float*>(p.residual) + o);
@@ -398,8 +492,10 @@ __global__ void __launch_bounds__(kThreads, 1) proj_tc_kernel(const __grid_const
           dst[i] = make_uint4(pack_half2(v[8 * i], v[8 * i + 1]), pack_half2(v[8 * i + 2], v[8 * i + 3]),
                               pack_half2(v[8 * i + 4], v[8 * i + 5]), pack_half2(v[8 * i + 6], v[8 * i + 7]));
       }
+      clear_acc(32 * c);
     }
   }
+  PRTRACE(5);
   griddep_launch_dependents();
   tc_fence_before();
   __syncthreads();
@@ -457,8 +553,8 @@ cudaError_t launch_proj_t(tla_ctx* ctx, ProjParams& p, cudaStream_t stream) {
   if (stages < 2) stages = 2;
   p.stages = stages;
   p.tmem_cols = p.NT <= 64 ? 64 : (p.NT <= 128 ? 128 : 256);
-  const int ring = stages * sb, epi = epilogue_bytes<D>(p.mode);
-  const int smem = (ring > epi ? ring : epi) + (2 * stages + 1) * 8 + 16 + 1024;
+  const int ring = stages * sb;
+  const int smem = region_bytes<D>(ring, p.mode) + (2 * stages + 1) * 8 + 16 + 1024;
   const void* k = reinterpret_cast<const void*>(proj_tc_kernel<D>);
   cudaError_t e = raise_smem_limit(k, smem);
   if (e != cudaSuccess) return e;
@@ -617,6 +713,10 @@ cudaError_t launch_qkv_proj(const tla_layer* L, const void* x, const void* weigh
   p.N = N;
   p.m_tiles = (rows + 127) / 128;
   p.NT = choose_nt(N, L->D, p.m_tiles, L->ctx->sm_count);
+#ifdef TLA_QKV_SPLIT_NT
+  if (p.m_tiles * (N / p.NT) < L->ctx->sm_count && N % TLA_QKV_SPLIT_NT == 0 && TLA_QKV_SPLIT_NT % L->D == 0)
+    p.NT = TLA_QKV_SPLIT_NT;
+#endif
   if (p.NT == 0) return cudaErrorInvalidValue;
   p.mode = prefill ? kQkvPrefill : kQkvDecode;
   p.bias = bias;
@@ -652,3 +752,10 @@ cudaError_t launch_out_proj(tla_ctx* ctx, const void* attn, const void* weight, 
 }
 
 }  // namespace tla
+
+#ifdef TLA_PROJ_TRACE
+extern "C" int tla_debug_proj_trace(unsigned long long* host, int count) {
+  return cudaMemcpyFromSymbol(host, tla::g_proj_trace, sizeof(unsigned long long) * count) == cudaSuccess ? 0 : -1;
+}
+#endif
+
