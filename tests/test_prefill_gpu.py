@@ -90,6 +90,27 @@ def test_prefill_sliding_window_and_qk_norm(pkg, cuda):
                  oracle_kw={"rope_theta": 10000.0, "sliding_window": 48, "q_norm_weight": qn, "k_norm_weight": kn})
 
 
+@pytest.mark.parametrize("dtype,window", [(torch.float16, 0), (torch.float32, 0), (torch.float16, 300)])
+def test_prefill_kv_range_pieces(pkg, cuda, dtype, window):
+    # One sequence, one kv head of 7 query heads, 1000 tokens after a 37-token
+    # prefix: 28 tile pairs for the SMs, so the head_dim-64 kernel cuts each
+    # pair's KV steps into pieces and merges their partial rows (with the gate)
+    kw = {"ropeTheta": 1e6}
+    okw = {"rope_theta": 1e6}
+    if window:
+        kw["slidingWindow"] = window
+        okw["sliding_window"] = window
+    prefill_case(pkg, cuda, 7, 1, 64, 1000, [37], 1100, dtype=dtype, gate=True, layer_kw=kw, oracle_kw=okw,
+                 seed=11)
+
+
+def test_prefill_config3_share_of_eight_gpus_vs_oracle(pkg, cuda):
+    # one rank's share of config 3 on eight GPUs: one sequence, one kv head and
+    # its 7 query heads, 2048 tokens (KV-range pieces)
+    prefill_case(pkg, cuda, 7, 1, 64, 2048, [0], 4096, layer_kw={"ropeTheta": 1e6}, oracle_kw={"rope_theta": 1e6},
+                 seed=12)
+
+
 def test_prefill_then_decode_continues(pkg, cuda):
     """Prefill S tokens, then decode the next one: same as S+1 reference steps."""
     rng = np.random.default_rng(9)

@@ -26,6 +26,11 @@ struct PrefillParams {
   int* error;
   int S, Hq, Hk, G, sliding, batch, num_m;
   float scale_log2;
+  // two-tile kernel: with piece_len > 0, each pair's KV steps are cut into
+  // pieces of about piece_len steps, every piece leaves fp32 partial rows in
+  // `part`, and a merge kernel writes the output (0: whole pairs)
+  int piece_len;
+  float* part;
 };
 
 // 2^x on the FMA pipe, for part of the softmax exponentials (the MUFU unit is the
@@ -147,6 +152,9 @@ inline CUresult make_map(const tla_layer* L, void* base, uint64_t rows, uint64_t
 cudaError_t pp_configure(const tla_layer* L);
 size_t pp_smem();
 cudaError_t launch_pp(const tla_layer* L, const PrefillParams& p, cudaStream_t stream);
+// Scratch bytes the two-tile kernel needs past the rotated queries for a
+// chunk of batch x seq_len (0: the chunk has enough work items unsplit).
+size_t pp_partial_bytes(const tla_layer* L, int batch, int seq_len);
 
 }  // namespace prefill
 }  // namespace tla

@@ -35,6 +35,9 @@
 // stops waiting and issuing, waits for the copies it issued, and frees TMEM.
 #include <limits.h>
 
+#include <algorithm>
+#include <vector>
+
 #include "prefill_common.cuh"
 
 namespace tla {
@@ -73,8 +76,8 @@ struct PP {
   static constexpr int kV = kK + kST * kTile;
   static constexpr int kOut = kV + kST * kTile;  // epilogue staging: 4 warps x 32 rows x D x up to 4 bytes
   static constexpr int kOutBytes = 4 * 32 * D * 4;
-  static constexpr int kL = kOut + kOutBytes;  // row sums [tile][item % 2][128] fp32
-  static constexpr int kBar = kL + 4 * 128 * 4;
+  static constexpr int kL = kOut + kOutBytes;  // row sums, then row maxima: [tile][item % 2][128] fp32 each
+  static constexpr int kBar = kL + 2 * 4 * 128 * 4;
   // q_full[4], q_empty[4], k_full, v_full, k_empty, v_empty [kST], s_full[2],
   // s_free[2], p_full[2], o_done[2], o_free[2], l_full[4]
   static constexpr int kNumBars = 8 + 4 * kST + 10 + 4;
@@ -102,14 +105,18 @@ __device__ __forceinline__ PairTile tile_of(const PairItem& w, int t) {
           z ? w.n[0] : w.n[1]};
 }
 
+__host__ __device__ __forceinline__ int pair_count(int G, int num_m, int batch, int Hk) {
+  return ((G * num_m + 1) / 2) * batch * Hk;
+}
 __device__ __forceinline__ int pair_count(const PrefillParams& p) {
-  return ((p.G * p.num_m + 1) / 2) * p.batch * p.Hk;
+  return pair_count(p.G, p.num_m, p.batch, p.Hk);
 }
 
-__device__ __forceinline__ PairItem pair_item(const PrefillParams& p, int it) {
+// Pair q (unsplit): units 2q and 2q + 1 of its (sequence, kv head) list.
+__device__ __forceinline__ PairItem pair_base(const PrefillParams& p, int q) {
   PairItem w;
   const int nbk = p.batch * p.Hk;
-  const int q = it / nbk, bk = it - q * nbk;
+  const int qq = q / nbk, bk = q - qq * nbk;
   w.b = bk / p.Hk;
   w.kvh = bk - w.b * p.Hk;
   w.start = p.start[w.b];
@@ -117,7 +124,7 @@ __device__ __forceinline__ PairItem pair_item(const PrefillParams& p, int it) {
   int lo = INT_MAX, hi = 0;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const int u = 2 * q + t;
+    const int u = 2 * qq + t;
     w.h[t] = w.row0[t] = w.rows[t] = w.j0[t] = w.n[t] = 0;
     if (u >= units) continue;
     const int mi = u / p.G;
@@ -135,7 +142,82 @@ __device__ __forceinline__ PairItem pair_item(const PrefillParams& p, int it) {
   return w;
 }
 
-template <typename OUT>
+// Pieces (piece_len > 0): pfx[q] = the first item of pair q, pfx[pairs] = the
+// number of items; each pair is cut into ceil(NJ / piece_len) pieces (at most
+// kMaxPieces). By the
+// block's threads (pairs <= kMaxPiecePairs), with a warp scan at the end.
+constexpr int kMaxPiecePairs = 320, kMaxPieces = 8, kMergeCols = 8;
+__device__ __forceinline__ void piece_prefix(const PrefillParams& p, int* pfx, int pairs) {
+  for (int q = threadIdx.x; q < pairs; q += blockDim.x) {
+    const int nj = pair_base(p, q).NJ;
+    pfx[q + 1] = min(kMaxPieces, max(1, (nj + p.piece_len - 1) / p.piece_len));
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {  // lane l takes a run of consecutive pairs, then a shuffle scan over the runs
+    constexpr int kRun = kMaxPiecePairs / 32;
+    const int lane = threadIdx.x, per = (pairs + 31) / 32;
+    const int q0 = min(pairs, lane * per), q1 = min(pairs, q0 + per);
+    int cts[kRun], run = 0;
+#pragma unroll
+    for (int i = 0; i < kRun; ++i) {
+      cts[i] = q0 + i < q1 ? pfx[q0 + i + 1] : 0;
+      run += cts[i];
+    }
+    __syncwarp();  // every count is read before any prefix overwrites it
+    int incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int acc = incl - run;  // this lane's exclusive prefix
+#pragma unroll
+    for (int i = 0; i < kRun; ++i) {
+      if (q0 + i < q1) pfx[q0 + i] = acc;
+      acc += cts[i];
+    }
+    if (lane == 31) pfx[pairs] = incl;  // the total (lanes past the last run add nothing)
+  }
+  __syncthreads();
+}
+
+// Work item `it`: pair it (piece_len == 0), or piece k of the pair q that
+// covers item it: steps [J0 + k NJ / c, J0 + (k + 1) NJ / c) of the pair's
+// union range (c pieces), each tile clipped to it (n[t] == 0: no step of the
+// tile in the piece).
+template <bool PIECES>
+__device__ __forceinline__ PairItem pair_item(const PrefillParams& p, int it, const int* pfx, int pairs) {
+  if constexpr (!PIECES) return pair_base(p, it);
+  int lo_q = 0, hi_q = pairs - 1;  // the last q with pfx[q] <= it
+  while (lo_q < hi_q) {
+    const int mid = (lo_q + hi_q + 1) >> 1;
+    if (pfx[mid] <= it)
+      lo_q = mid;
+    else
+      hi_q = mid - 1;
+  }
+  PairItem w = pair_base(p, lo_q);
+  const int k = it - pfx[lo_q], c = pfx[lo_q + 1] - pfx[lo_q];
+  const int p0 = w.J0 + (k * w.NJ) / c, p1 = w.J0 + ((k + 1) * w.NJ) / c;
+  int lo = INT_MAX, hi = 0;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int a = max(w.j0[t], p0), e = min(w.j0[t] + w.n[t], p1);
+    if (w.n[t] == 0 || e <= a) {
+      w.n[t] = 0;
+      continue;
+    }
+    w.j0[t] = a;
+    w.n[t] = e - a;
+    lo = min(lo, a);
+    hi = max(hi, e);
+  }
+  w.J0 = hi == 0 ? 0 : lo;  // (an empty piece: NJ = 0)
+  w.NJ = hi - w.J0;
+  return w;
+}
+
+template <typename OUT, bool PIECES>
 __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __grid_constant__ PrefillParams p) {
   constexpr int kT = 128, D = PP::D;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -157,7 +239,8 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + PP::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* l_buf = reinterpret_cast<float*>(smem + PP::kL);  // [2 t + item % 2][128]
-  const int num_items = pair_count(p);
+  const int pairs = pair_count(p);
+  __shared__ int pfx[kMaxPiecePairs + 1];  // pieces: the first item of each pair
 #ifdef TLA_PREFILL_TRACE
   if (tid == 0 && blockIdx.x < 256) g_pp_cta[blockIdx.x][0] = globaltimer();
 #endif
@@ -190,6 +273,13 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
 #ifdef TLA_PREFILL_TRACE
   if (tid == 0 && blockIdx.x < 256) g_pp_cta[blockIdx.x][1] = globaltimer();
 #endif
+  if constexpr (PIECES) {
+    piece_prefix(p, pfx, pairs);  // (the start positions may come from the kernel before)
+    // the merge kernel may launch now: it builds its piece table, then waits
+    // for this grid to complete (its CTAs take the SMs this grid leaves)
+    griddep_launch_dependents();
+  }
+  const int num_items = PIECES ? pfx[pairs] : pairs;
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     if (*abort_flag) return;
     if (!mbar_wait(bar, parity, p.error)) *abort_flag = 1;
@@ -213,7 +303,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
       for (int k = 0;; ++k) {
         const int it = prefill_item_of(k, num_items);
         if (it < 0) break;
-        const PairItem w = pair_item(p, it);
+        const PairItem w = pair_item<PIECES>(p, it, pfx, pairs);
         if (lane == 0) {
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
@@ -259,7 +349,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
         for (int k = 0;; ++k) {
           const int it = prefill_item_of(k, num_items);
           if (it < 0) break;
-          const PairItem w = pair_item(p, it);
+          const PairItem w = pair_item<PIECES>(p, it, pfx, pairs);
           for (int n = 0; n < w.NJ; ++n, ++g) {
             const int st = g % PP::kST, J = w.J0 + n;
             spin(&k_full[st], (g / PP::kST) & 1);
@@ -297,7 +387,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
         for (int k = 0;; ++k) {
           const int it = prefill_item_of(k, num_items);
           if (it < 0) break;
-          const PairItem w = pair_item(p, it);
+          const PairItem w = pair_item<PIECES>(p, it, pfx, pairs);
           for (int n = 0; n < w.NJ; ++n, ++g) {
             const int st = g % PP::kST, J = w.J0 + n;
             spin(&v_full[st], (g / PP::kST) & 1);
@@ -344,7 +434,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
     for (int k = 0;; ++k) {
       const int it = prefill_item_of(k, num_items);
       if (it < 0) break;
-      const PairItem w = pair_item(p, it);
+      const PairItem w = pair_item<PIECES>(p, it, pfx, pairs);
 #pragma unroll 1
       for (int t = 0; t < 2; ++t) {
         const PairTile u = tile_of(w, t);
@@ -362,76 +452,99 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
         const long long base = ((static_cast<long long>(w.b) * p.S + u.row0) * p.Hq + u.h) * D;
         const int rows = u.rows;
         const uint32_t oe = tmem + lane_base + PP::kO + 64 * t;
+        if constexpr (PIECES) {
+          // a piece: the row's unnormalised O, its maximum and its sum, fp32,
+          // column-major per (item, tile) block [D + 2][128] so that a warp's
+          // rows are 32 consecutive words (the merge kernel writes the output)
+          float* dst = p.part + (static_cast<size_t>(it) * 2 + t) * (D + 2) * 128 + r;
 #pragma unroll 1
-        for (int cc = 0; cc < D / 16; ++cc) {  // 16 columns at a time
-          uint32_t ou[16];
-          tmem_ld16(oe + 16 * cc, ou);
-          float o[16];
+          for (int cc = 0; cc < D / 16; ++cc) {
+            uint32_t ou[16];
+            tmem_ld16(oe + 16 * cc, ou);
+            if (r < rows) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(ou[i]) * inv;
-          // output gate (TSLAttention.ts:418-423, math.ts:271-273): times
-          // sigmoid(gate) in fp32 before the conversion to OUT
-          if (p.gate != nullptr && r < rows &&
-              TLA_IN_BOUNDS(base + r * row_stride + 16 * cc + 15, out_elems, p.error)) {
-            const OUT* gsrc = static_cast<const OUT*>(p.gate) + base + r * row_stride + 16 * cc;
+              for (int i = 0; i < 16; ++i) dst[(16 * cc + i) * 128] = __uint_as_float(ou[i]);
+            }
+          }
+          if (r < rows) {
+            dst[D * 128] = l_buf[512 + slot * 128 + r];
+            dst[(D + 1) * 128] = le;
+          }
+          tc_fence_before();
+          mbar_arrive(&o_free[t]);
+          ++kt;
+        } else {
+#pragma unroll 1
+          for (int cc = 0; cc < D / 16; ++cc) {  // 16 columns at a time
+            uint32_t ou[16];
+            tmem_ld16(oe + 16 * cc, ou);
+            float o[16];
 #pragma unroll
-            for (int i0 = 0; i0 < 16; i0 += 8) {
-              float gv[8];
-              if constexpr (sizeof(OUT) == 2) {
-                const uint4 u = *reinterpret_cast<const uint4*>(gsrc + i0);
-                const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+            for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(ou[i]) * inv;
+            // output gate (TSLAttention.ts:418-423, math.ts:271-273): times
+            // sigmoid(gate) in fp32 before the conversion to OUT
+            if (p.gate != nullptr && r < rows &&
+                TLA_IN_BOUNDS(base + r * row_stride + 16 * cc + 15, out_elems, p.error)) {
+              const OUT* gsrc = static_cast<const OUT*>(p.gate) + base + r * row_stride + 16 * cc;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  gv[2 * j] = __low2float(h2[j]);
-                  gv[2 * j + 1] = __high2float(h2[j]);
+              for (int i0 = 0; i0 < 16; i0 += 8) {
+                float gv[8];
+                if constexpr (sizeof(OUT) == 2) {
+                  const uint4 u = *reinterpret_cast<const uint4*>(gsrc + i0);
+                  const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    gv[2 * j] = __low2float(h2[j]);
+                    gv[2 * j + 1] = __high2float(h2[j]);
+                  }
+                } else {
+                  const float4 a = *reinterpret_cast<const float4*>(gsrc + i0);
+                  const float4 b = *reinterpret_cast<const float4*>(gsrc + i0 + 4);
+                  gv[0] = a.x, gv[1] = a.y, gv[2] = a.z, gv[3] = a.w;
+                  gv[4] = b.x, gv[5] = b.y, gv[6] = b.z, gv[7] = b.w;
                 }
-              } else {
-                const float4 a = *reinterpret_cast<const float4*>(gsrc + i0);
-                const float4 b = *reinterpret_cast<const float4*>(gsrc + i0 + 4);
-                gv[0] = a.x, gv[1] = a.y, gv[2] = a.z, gv[3] = a.w;
-                gv[4] = b.x, gv[5] = b.y, gv[6] = b.z, gv[7] = b.w;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o[i0 + j] *= 1.f / (1.f + expf(-gv[j]));
               }
+            }
+            // into the stage: 16-byte chunks XOR-swizzled by row
+            constexpr int kPer16 = static_cast<int>(sizeof(OUT));  // 16-byte chunks per 16 values
 #pragma unroll
-              for (int j = 0; j < 8; ++j) o[i0 + j] *= 1.f / (1.f + expf(-gv[j]));
+            for (int i = 0; i < kPer16; ++i) {
+              uint4 v;
+              if constexpr (sizeof(OUT) == 2) {
+                const float* f = o + 8 * i;
+                v = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
+                               pack_half2(f[6], f[7]));
+              } else {
+                const float* f = o + 4 * i;
+                v = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                               __float_as_uint(f[3]));
+              }
+              const int q = cc * kPer16 + i;
+              *reinterpret_cast<uint4*>(stage + lane * kRowBytes + ((q ^ (lane & 7)) << 4)) = v;
             }
           }
-          // into the stage: 16-byte chunks XOR-swizzled by row
-          constexpr int kPer16 = static_cast<int>(sizeof(OUT));  // 16-byte chunks per 16 values
-#pragma unroll
-          for (int i = 0; i < kPer16; ++i) {
-            uint4 v;
-            if constexpr (sizeof(OUT) == 2) {
-              const float* f = o + 8 * i;
-              v = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
-                             pack_half2(f[6], f[7]));
-            } else {
-              const float* f = o + 4 * i;
-              v = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
-                             __float_as_uint(f[3]));
-            }
-            const int q = cc * kPer16 + i;
-            *reinterpret_cast<uint4*>(stage + lane * kRowBytes + ((q ^ (lane & 7)) << 4)) = v;
-          }
-        }
-        // O has been read: the tile's next item may start accumulating
-        tc_fence_before();
-        mbar_arrive(&o_free[t]);
-        ++kt;
-        __syncwarp();
-        // whole rows out: a warp-wide store covers kRowsPer rows
-        const int q = lane % kChunks;
-        const uint8_t* src = stage + (lane / kChunks) * kRowBytes;
-        int row = (warp & 3) * 32 + lane / kChunks;
-        uint8_t* dst = reinterpret_cast<uint8_t*>(static_cast<OUT*>(p.out) + base + row * row_stride) + (q << 4);
-        const size_t dst_step = kRowsPer * row_stride * sizeof(OUT);
+          // O has been read: the tile's next item may start accumulating
+          tc_fence_before();
+          mbar_arrive(&o_free[t]);
+          ++kt;
+          __syncwarp();
+          // whole rows out: a warp-wide store covers kRowsPer rows
+          const int q = lane % kChunks;
+          const uint8_t* src = stage + (lane / kChunks) * kRowBytes;
+          int row = (warp & 3) * 32 + lane / kChunks;
+          uint8_t* dst = reinterpret_cast<uint8_t*>(static_cast<OUT*>(p.out) + base + row * row_stride) + (q << 4);
+          const size_t dst_step = kRowsPer * row_stride * sizeof(OUT);
 #pragma unroll 1
-        for (int i = 0; i < kChunks; ++i, row += kRowsPer, src += kRowsPer * kRowBytes, dst += dst_step) {
-          const uint4 v = *reinterpret_cast<const uint4*>(src + ((q ^ (row & 7)) << 4));
-          if (row < rows && TLA_IN_BOUNDS(base + row * row_stride + ((q + 1) * 16) / sizeof(OUT) - 1, out_elems,
-                                          p.error))
-            *reinterpret_cast<uint4*>(dst) = v;
+          for (int i = 0; i < kChunks; ++i, row += kRowsPer, src += kRowsPer * kRowBytes, dst += dst_step) {
+            const uint4 v = *reinterpret_cast<const uint4*>(src + ((q ^ (row & 7)) << 4));
+            if (row < rows && TLA_IN_BOUNDS(base + row * row_stride + ((q + 1) * 16) / sizeof(OUT) - 1, out_elems,
+                                            p.error))
+              *reinterpret_cast<uint4*>(dst) = v;
+          }
+          __syncwarp();  // the stage is reused by the next tile
         }
-        __syncwarp();  // the stage is reused by the next tile
       }
     }
   } else {
@@ -449,7 +562,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
     for (int k = 0;; ++k) {
       const int it = prefill_item_of(k, num_items);
       if (it < 0) break;
-      const PairItem w = pair_item(p, it);
+      const PairItem w = pair_item<PIECES>(p, it, pfx, pairs);
       const PairTile u = tile_of(w, t);
       if (u.n == 0) continue;
       const int pr = w.start + u.row0 + r;
@@ -550,6 +663,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
       // the row sum for the epilogue
       const int slot = 2 * t + (kq & 1);
       l_buf[slot * 128 + r] = l_run;
+      l_buf[512 + slot * 128 + r] = m_run;  // (read only for partial rows)
       mbar_arrive(&l_full[slot]);
       ++kq;
     }
@@ -571,6 +685,91 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
 #endif
 }
 
+// Merge of the KV-range pieces (piece_len > 0): one CTA per (pair, tile,
+// group of kMergeCols columns), a thread per output row, whose pieces' loads
+// all go out in one round (the partial blocks are column-major, so a warp's
+// loads are 32 consecutive words). The pieces' unnormalised (O, m, l) combine
+// by the log-sum-exp rule (m in the log2 domain), then O / l times the output
+// gate (TSLAttention.ts:418-423) goes out.
+template <typename OUT>
+__global__ void __launch_bounds__(128) prefill_pp_merge_kernel(const __grid_constant__ PrefillParams p) {
+  constexpr int D = PP::D, kCols = kMergeCols;
+  __shared__ int pfx[kMaxPiecePairs + 1];
+  __shared__ int in_piece[kMaxPieces];  // the tile has steps in piece k
+  __shared__ int tile_b, tile_row0, tile_h, tile_rows;
+  const int r = threadIdx.x;
+  const int col0 = (static_cast<int>(blockIdx.x) % (D / kCols)) * kCols;
+  const int pt = static_cast<int>(blockIdx.x) / (D / kCols);
+  const int pq = pt >> 1, t = pt & 1;
+  const int pairs = pair_count(p);
+  // The piece table before the wait: the start positions were final before
+  // the attention kernel started (it waited for them itself).
+  piece_prefix(p, pfx, pairs);
+  const int first = pfx[pq], pieces = pfx[pq + 1] - first;
+  if (r == 0) {
+    const PairItem w = pair_base(p, pq);
+    const PairTile u = tile_of(w, t);
+    tile_b = w.b;
+    tile_row0 = u.row0;
+    tile_h = u.h;
+    tile_rows = u.rows;
+    for (int k = 0; k < kMaxPieces; ++k) {  // as pair_item cuts the pieces
+      const int p0 = w.J0 + (k * w.NJ) / max(pieces, 1), p1 = w.J0 + ((k + 1) * w.NJ) / max(pieces, 1);
+      in_piece[k] = k < pieces && min(u.j0 + u.n, p1) > max(u.j0, p0);
+    }
+  }
+  __syncthreads();
+  griddep_wait();  // the pieces are complete and visible
+  if (r >= tile_rows) return;
+  constexpr size_t kBlock = static_cast<size_t>(D + 2) * 128;  // floats of one (item, tile) block
+  const float* rowp = p.part + static_cast<size_t>(first * 2 + t) * kBlock + r;
+  float mk[kMaxPieces], lk[kMaxPieces], ok[kMaxPieces][kCols];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < kMaxPieces; ++k) {
+    const float* src = rowp + k * 2 * kBlock;
+    const bool in = in_piece[k] != 0;
+    mk[k] = in ? __ldcg(src + D * 128) : -INFINITY;
+    lk[k] = in ? __ldcg(src + (D + 1) * 128) : 0.f;
+#pragma unroll
+    for (int i = 0; i < kCols; ++i) ok[k][i] = in ? __ldcg(src + (col0 + i) * 128) : 0.f;
+    mx = fmaxf(mx, mk[k]);
+  }
+  float acc[kCols];
+#pragma unroll
+  for (int i = 0; i < kCols; ++i) acc[i] = 0.f;
+  float l = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxPieces; ++k) {
+    // (not in the piece, or no unmasked column of the row there: weight 0)
+    const float f = mk[k] == -INFINITY ? 0.f : ex2(mk[k] - mx);
+    l += f * lk[k];
+#pragma unroll
+    for (int i = 0; i < kCols; ++i) acc[i] += f * ok[k][i];
+  }
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  const long long base = ((static_cast<long long>(tile_b) * p.S + tile_row0 + r) * p.Hq + tile_h) * D + col0;
+  if (!TLA_IN_BOUNDS(base + kCols - 1, static_cast<long long>(p.batch) * p.S * p.Hq * D, p.error)) return;
+  const OUT* gs = p.gate != nullptr ? static_cast<const OUT*>(p.gate) + base : nullptr;
+  OUT* dst = static_cast<OUT*>(p.out) + base;
+#pragma unroll
+  for (int i = 0; i < kCols; i += 8) {
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      o[j] = acc[i + j] * inv;
+      if (gs != nullptr) o[j] *= 1.f / (1.f + expf(-to_f32(gs[i + j])));  // in fp32 before the conversion
+    }
+    if constexpr (sizeof(OUT) == 2) {
+      *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]),
+                                                      pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
+    } else {
+      *reinterpret_cast<float4*>(dst + i) = make_float4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<float4*>(dst + i + 4) = make_float4(o[4], o[5], o[6], o[7]);
+    }
+  }
+}
+
 }  // namespace
 
 namespace prefill {
@@ -585,17 +784,79 @@ extern "C" int tla_debug_pp_cta(unsigned long long* host, int count) {
 #endif
 
 cudaError_t pp_configure(const tla_layer* L) {
-  return L->io_fp32 ? raise_smem_limit(reinterpret_cast<const void*>(prefill_pp_kernel<float>), PP::kSmem)
-                    : raise_smem_limit(reinterpret_cast<const void*>(prefill_pp_kernel<__half>), PP::kSmem);
+  cudaError_t e = L->io_fp32
+                      ? raise_smem_limit(reinterpret_cast<const void*>(prefill_pp_kernel<float, false>), PP::kSmem)
+                      : raise_smem_limit(reinterpret_cast<const void*>(prefill_pp_kernel<__half, false>), PP::kSmem);
+  if (e != cudaSuccess) return e;
+  return L->io_fp32 ? raise_smem_limit(reinterpret_cast<const void*>(prefill_pp_kernel<float, true>), PP::kSmem)
+                    : raise_smem_limit(reinterpret_cast<const void*>(prefill_pp_kernel<__half, true>), PP::kSmem);
 }
 
 size_t pp_smem() { return PP::kSmem; }
 
-cudaError_t launch_pp(const tla_layer* L, const PrefillParams& p, cudaStream_t stream) {
-  const int items = ((p.G * p.num_m + 1) / 2) * p.batch * p.Hk;
-  const unsigned grid = static_cast<unsigned>(items < L->ctx->sm_count ? items : L->ctx->sm_count);
-  if (L->io_fp32) return launch_pdl(prefill_pp_kernel<float>, grid, PP::kThreads, PP::kSmem, stream, p);
-  return launch_pdl(prefill_pp_kernel<__half>, grid, PP::kThreads, PP::kSmem, stream, p);
+// Piece length (KV steps) for a chunk, 0 for whole pairs. Each piece costs a
+// query-tile load, a first step from cold, a partial-row epilogue and a share
+// of the merge kernel, so the chunk is cut only when it has at most one pair
+// per two SMs (measured: one pair per SM gained nothing), and then into the
+// longest pieces that still fit in one wave of items: the smallest length L
+// with sum over pairs of min(kMaxPieces, ceil(NJ / L)) <= SMs, the pairs'
+// step counts NJ taken at start position 0.
+int pp_piece_len(const tla_layer* L, int batch, int seq_len) {
+  const int num_m = (seq_len + 127) / 128, G = L->G;
+  const long long pairs = pair_count(G, num_m, batch, L->Hk);
+  const int sms = L->ctx->sm_count;
+  if (pairs <= 0 || sms <= 0 || 2 * pairs > sms || pairs > kMaxPiecePairs) return 0;
+  // step counts of one (sequence, kv head)'s pairs (the same for all of them at start 0)
+  const int units = G * num_m, per = (units + 1) / 2;
+  std::vector<int> nj(per);
+  int max_nj = 0;
+  for (int q = 0; q < per; ++q) {
+    int lo = 1 << 30, hi = 0;
+    for (int u = 2 * q; u < 2 * q + 2 && u < units; ++u) {
+      const int row0 = (num_m - 1 - u / G) * 128, rows = std::min(128, seq_len - row0);
+      const int j0 = (L->sliding > 0 ? std::max(0, row0 - L->sliding + 1) : 0) / 128;
+      lo = std::min(lo, j0);
+      hi = std::max(hi, (row0 + rows - 1) / 128 + 1);
+    }
+    nj[q] = hi - lo;
+    max_nj = std::max(max_nj, nj[q]);
+  }
+  const long long copies = pairs / per;  // (sequence, kv head) lists
+  for (int len = 2; len < max_nj; ++len) {
+    long long items = 0;
+    for (int q = 0; q < per; ++q) items += std::min(kMaxPieces, (nj[q] + len - 1) / len);
+    if (items * copies <= sms) return len;
+  }
+  return 0;
+}
+
+size_t pp_partial_bytes(const tla_layer* L, int batch, int seq_len) {
+  if (pp_piece_len(L, batch, seq_len) == 0) return 0;
+  const int pairs = pair_count(L->G, (seq_len + 127) / 128, batch, L->Hk);
+  return static_cast<size_t>(pairs) * kMaxPieces * 2 * (PP::D + 2) * 128 * sizeof(float);
+}
+
+cudaError_t launch_pp(const tla_layer* L, const PrefillParams& p0, cudaStream_t stream) {
+  PrefillParams p = p0;
+  const int pairs = pair_count(p.G, p.num_m, p.batch, p.Hk);
+  p.piece_len = pp_piece_len(L, p.batch, p.S);
+  // the pieces' partial blocks follow the rotated queries [B][Hq][S][D] fp16 in the query scratch
+  const size_t q_bytes = (static_cast<size_t>(p.batch) * p.Hq * p.S * PP::D * sizeof(__half) + 255) & ~size_t(255);
+  p.part = p.piece_len > 0 ? reinterpret_cast<float*>(static_cast<uint8_t*>(L->ctx->d_qscratch) + q_bytes) : nullptr;
+  const int sms = L->ctx->sm_count;
+  const unsigned grid = static_cast<unsigned>(p.piece_len > 0 ? sms : (pairs < sms ? pairs : sms));
+  // (pieces get their own instance, so that whole-pair chunks run the kernel without the piece code)
+  cudaError_t e;
+  if (p.piece_len > 0)
+    e = L->io_fp32 ? launch_pdl(prefill_pp_kernel<float, true>, grid, PP::kThreads, PP::kSmem, stream, p)
+                   : launch_pdl(prefill_pp_kernel<__half, true>, grid, PP::kThreads, PP::kSmem, stream, p);
+  else
+    e = L->io_fp32 ? launch_pdl(prefill_pp_kernel<float, false>, grid, PP::kThreads, PP::kSmem, stream, p)
+                   : launch_pdl(prefill_pp_kernel<__half, false>, grid, PP::kThreads, PP::kSmem, stream, p);
+  if (e != cudaSuccess || p.piece_len == 0) return e;
+  const unsigned mgrid = static_cast<unsigned>(pairs) * 2 * (PP::D / kMergeCols);  // a CTA per (pair, tile, columns)
+  return L->io_fp32 ? launch_pdl(prefill_pp_merge_kernel<float>, mgrid, 128, 0, stream, p)
+                    : launch_pdl(prefill_pp_merge_kernel<__half>, mgrid, 128, 0, stream, p);
 }
 
 }  // namespace prefill

@@ -715,6 +715,11 @@ cudaError_t prefill_fast_configure(tla_layer* L) {
   return cudaSuccess;
 }
 
+size_t prefill_scratch_bytes(const tla_layer* L, int batch, int seq_len) {
+  const size_t q = (static_cast<size_t>(batch) * L->Hq * seq_len * L->D * sizeof(__half) + 255) & ~size_t(255);
+  return q + ((L->D == 64 && TLA_PREFILL_PP && L->fast_prefill) ? pp_partial_bytes(L, batch, seq_len) : 0);
+}
+
 cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32_t* start, const void* gate, int batch,
                                 int seq_len, void* out, cudaStream_t stream) {
   __half* qh = static_cast<__half*>(L->ctx->d_qscratch);
@@ -735,6 +740,8 @@ cudaError_t launch_prefill_attention(const tla_layer* L, const int32_t* start, c
   p.gate = gate;
   p.start = start;
   p.error = L->ctx->d_error;
+  p.piece_len = 0;
+  p.part = nullptr;
   p.S = seq_len;
   p.Hq = L->Hq;
   p.Hk = L->Hk;

@@ -475,7 +475,7 @@ int tla_prefill(tla_layer* L, const void* qkv, const int32_t* start_pos, const v
   DeviceGuard g(L->ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (L->fast_prefill && !L->borrowed) {
-    int rc = ensure_qscratch(L->ctx, static_cast<size_t>(batch) * seq_len * L->Hq * L->D * sizeof(__half));
+    int rc = ensure_qscratch(L->ctx, tla::prefill_scratch_bytes(L, batch, seq_len));
     if (rc != TLA_OK) return rc;
     return from_cuda(tla::launch_prefill_fast(L, qkv, start_pos, gate, batch, seq_len, out, st));
   }
@@ -516,7 +516,7 @@ int tla_qkv_prefill(tla_layer* L, const void* x, const void* weight, const float
   if (L->borrowed) return TLA_ERR_SHARED;
   if (batch == 0 || seq_len == 0) return TLA_OK;
   DeviceGuard g(L->ctx->device);
-  int rc = ensure_qscratch(L->ctx, static_cast<size_t>(batch) * seq_len * L->Hq * L->D * sizeof(__half));
+  int rc = ensure_qscratch(L->ctx, tla::prefill_scratch_bytes(L, batch, seq_len));
   if (rc != TLA_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   __half* q = static_cast<__half*>(L->ctx->d_qscratch);

@@ -148,6 +148,10 @@ cudaError_t launch_prefill_fast(const tla_layer* L, const void* qkv, const int32
 
 // The causal attention kernel alone, over rotated queries already in the
 // context's query scratch ([B][Hq][S][D] fp16) and K/V already appended.
+// Query scratch bytes the tensor-core prefill of a chunk needs: the rotated
+// queries [B][Hq][S][D] fp16 (rounded up to 256 bytes), then, when the chunk
+// is split into KV-range pieces, their partial rows.
+size_t prefill_scratch_bytes(const tla_layer* L, int batch, int seq_len);
 cudaError_t launch_prefill_attention(const tla_layer* L, const int32_t* start, const void* gate, int batch,
                                      int seq_len, void* out, cudaStream_t stream);
 // Decode over rotated queries [B][Hq][D] fp16 whose new K/V rows are already
