@@ -162,13 +162,20 @@ __device__ __forceinline__ void seq_range(const LayerArgs& a, int pos, int slot_
   *hi = min(pos, slot_offset + local_tokens - 1) - slot_offset;
 }
 
+// First unit of CTA c. The set-up runs it a few times on its critical path:
+// a 32-bit division when c * total fits (c <= grid <= 16 D <= 4096), else
+// 64-bit.
 __device__ __forceinline__ long long cta_begin(int c, long long total, int grid) {
+  if (total < (1LL << 31) / 4096)
+    return static_cast<long long>(static_cast<unsigned>(c * static_cast<int>(total)) / static_cast<unsigned>(grid));
   return (static_cast<long long>(c) * total) / grid;
 }
 
 // Largest c with cta_begin(c) <= g.
 __device__ __forceinline__ int cta_of(long long g, long long total, int grid) {
-  int c = static_cast<int>((g * grid) / total);
+  int c = total < (1LL << 31) / 4096
+              ? static_cast<int>(static_cast<unsigned>(static_cast<int>(g) * grid) / static_cast<unsigned>(total))
+              : static_cast<int>((g * grid) / total);
   while (c + 1 < grid && cta_begin(c + 1, total, grid) <= g) ++c;
   while (c > 0 && cta_begin(c, total, grid) > g) --c;
   return c;
@@ -196,9 +203,10 @@ struct Seg {
 template <typename PT>
 __device__ __forceinline__ Seg seg_at(const PT* prefix, int b, int Hk, int setup, long long g, long long te) {
   Seg sg;
-  const int per = static_cast<int>((prefix[b + 1] - prefix[b]) / Hk);  // units per pair: tiles + setup
+  // (a sequence's units fit in 32 bits: Hk * (max_tokens / 64 + setup))
+  const int per = static_cast<int>(prefix[b + 1] - prefix[b]) / Hk;  // units per pair: tiles + setup
   sg.tiles = per - setup;
-  sg.kvh = static_cast<int>((g - prefix[b]) / per);
+  sg.kvh = static_cast<int>(g - prefix[b]) / per;
   sg.start = prefix[b] + static_cast<long long>(sg.kvh) * per;
   sg.first_tile = sg.start + setup;
   const long long end = min(te, sg.first_tile + sg.tiles);
