@@ -114,6 +114,7 @@ struct DecodeParams {
   long long scratch_floats, counter_count;  // extents (bounds-check builds)
   int batch, slot_offset, local_tokens, append;
   int defer_merge;  // 1: split pairs are merged by decode_merge_kernel instead of the last CTA
+  int small_grid;   // CTAs for a small launch (one per SM; 0: always the whole grid), see effective_grid
 };
 
 struct SmemLayout {
@@ -169,6 +170,14 @@ __device__ __forceinline__ long long cta_begin(int c, long long total, int grid)
   if (total < (1LL << 31) / 4096)
     return static_cast<long long>(static_cast<unsigned>(c * static_cast<int>(total)) / static_cast<unsigned>(grid));
   return (static_cast<long long>(c) * total) / grid;
+}
+
+// CTAs that take part in a launch of `total` units: a small launch (fewer
+// than 8 units per SM) runs on one CTA per SM, so each CTA streams more tiles
+// and a pair is cut into fewer segments (measured: config 2 at batch 1); the
+// decode, merge and exchange kernels all derive it from the same total.
+__device__ __forceinline__ int effective_grid(long long total, int grid, int small) {
+  return (small > 0 && small < grid && total < 8LL * small) ? small : grid;
 }
 
 // Largest c with cta_begin(c) <= g.
@@ -335,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
   uint64_t* empty = full + C::kStages;
   volatile int* flags = reinterpret_cast<volatile int*>(smem + L.flags);  // [0] abort, [1] last-CTA ticket
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int grid = gridDim.x, cta = blockIdx.x;
+  const int launch_grid = gridDim.x, cta = blockIdx.x;
   if (tid == 0) DTRACE(0);
   if (tid == 0) {
     flags[0] = 0;
@@ -357,10 +366,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
   __syncthreads();
   scan_prefix(prefix, p.batch, warp, lane);
   __syncthreads();
+  int grid = effective_grid(prefix[p.batch], launch_grid, p.small_grid);
   if (warp == kConsumerWarps) {
-    if (lane == 0) prefetch_first_tiles<D>(p, prefix, cta, grid);
+    if (lane == 0 && cta < grid) prefetch_first_tiles<D>(p, prefix, cta, grid);
   } else {
-    prefetch_first_rows<D, IO>(p, prefix, cta, grid, tid);
+    if (cta < grid) prefetch_first_rows<D, IO>(p, prefix, cta, grid, tid);
     // rows G..15 of the query tile stay zero (the m16 MMA's padding rows)
     __half* q_pad = reinterpret_cast<__half*>(smem + L.q);
     for (int i = tid; i < (16 - G) * D; i += kConsumerWarps * 32) {
@@ -390,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
   }
   if (tid == 0) DTRACE(14);
   const long long total = prefix[p.batch];
+  grid = effective_grid(total, launch_grid, p.small_grid);
 
   // Sequence-shard mode: pairs with no local tokens still emit an empty triple.
   if (p.partial_out != nullptr) {
@@ -402,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::kMinBlocks)
     }
   }
   if (tid == 0) DTRACE(1);
-  if (total == 0) return;
+  if (total == 0 || cta >= grid) return;  // (CTAs past a small launch's grid have no units)
   const long long tb = cta_begin(cta, total, grid);
   const long long te = cta_begin(cta + 1, total, grid);
   if (tb >= te) return;
@@ -963,6 +974,7 @@ __global__ void __launch_bounds__(NT) decode_merge_kernel(const __grid_constant_
   }
   __syncthreads();
   const long long total = prefix[p.batch];
+  grid = effective_grid(total, grid, p.small_grid);  // as the decode kernel took it
   if (prefix[b + 1] == prefix[b]) return;  // no tiles
   const Seg sg = seg_at(prefix, b, Hk, Units<D>::kSetup, prefix[b] + (prefix[b + 1] - prefix[b]) / Hk * kvh, total);
   const int tiles = sg.tiles;
@@ -1125,6 +1137,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_exchange_kernel(const __
   griddep_launch_dependents();
   const unsigned epoch = xch_epoch(x, &epoch_s);  // syncs the block
   const long long total = prefix[p.batch];
+  grid = effective_grid(total, grid, p.small_grid);  // as the decode kernel took it
   const int rows = p.batch * Hq;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const int b = row / Hq, h = row - b * Hq, kvh = h / G, r = h - kvh * G;
@@ -1345,6 +1358,7 @@ DecodeParams decode_params(const tla_layer* L, const void* qkv, const int32_t* p
   // Few, long sequences split each (sequence, kv head) over many CTAs: merge
   // those in a separate, fully parallel kernel instead of in the last CTA.
   p.defer_merge = L->decode_grid > TLA_DEFER_MERGE_SEGMENTS * batch * L->Hk ? 1 : 0;
+  p.small_grid = L->decode_grid > L->ctx->sm_count ? L->ctx->sm_count : 0;
   return p;
 }
 }  // namespace
