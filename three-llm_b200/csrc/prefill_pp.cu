@@ -12,11 +12,14 @@
 // next S of a tile is computed while that tile's exponentials run.
 //
 // Warp roles (512 threads):
-//   warps 0-3 / 4-7  softmax of tile 0 / 1 (thread = query row = TMEM lane)
-//   warps 8-11       epilogue: O / l, the output gate, rows out via shared memory
-//   warp 12          TMA: lane 0 the Q tiles and K steps, lane 1 the V steps
-//   warp 13          S issuer (both tiles), warp 15 P V issuer (both tiles)
-//   warp 14          TMEM owner
+//   warp 0           TMA: lane 0 the Q tiles and K steps, lane 1 the V steps
+//   warp 1           S issuer (both tiles), warp 3 P V issuer (both tiles)
+//   warp 2           TMEM owner
+//   warps 4-7 / 8-11 softmax of tile 0 / 1 (thread = query row = TMEM lane)
+//   warps 12-15      epilogue: O / l, the output gate, rows out via shared memory
+// A sub-partition runs warps w, w + 4, w + 8 and w + 12; a busy softmax pair
+// beside an MMA issuer slows its issue (an M=128 N=64 MMA: 45 cycles alone,
+// 55-85 with such neighbours), so the issuers' latency shows in each step.
 // Registers: the launch gives 128 per thread; setmaxnreg moves them to the
 // softmax warpgroups (184) from the epilogue (88) and control (56) warpgroups:
 // 2 x 184 + 88 + 56 = 512 = 4 x 128.
@@ -83,7 +86,11 @@ struct PP {
   static constexpr int kNumBars = 8 + 4 * kST + 10 + 4;
   static constexpr int kSmem = kBar + kNumBars * 8 + 16 + 1024;
   static constexpr uint32_t kS = 0, kP = 256, kO = 384, kCols = 512;
-  static constexpr int kAllocWarp = 14;
+  // warpgroups by role: the MMA issuers and the TMA warp as warps 0-3 took
+  // config 3 from 0.0799 to 0.0787 ms against warps 12-15
+  static constexpr int kCtrlWg = 0, kSoftWg0 = 1, kEpiWg = 3;
+  static constexpr int kTmaWarp = 4 * kCtrlWg, kSWarp = kTmaWarp + 1, kAllocWarp = kTmaWarp + 2,
+                       kPvWarp = kTmaWarp + 3;
 };
 static_assert(PP::kSmem <= 232448, "shared memory");
 
@@ -287,11 +294,13 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
   auto spin = [&](uint64_t* bar, uint32_t parity) {
     if (!*abort_flag && !mbar_spin(bar, parity, p.error)) *abort_flag = 1;
   };
-  const int wg = warp >> 2;
 
-  if (wg == 3) {
+  const int wg = warp >> 2;
+  const int role = wg == PP::kCtrlWg ? 3 : wg == PP::kEpiWg ? 2 : wg - PP::kSoftWg0;  // 0 / 1 softmax of tile 0 / 1
+
+  if (role == 3) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
-    if (warp == 12 && lane < 2) {
+    if (warp == PP::kTmaWarp && lane < 2) {
       // ============================================================ TMA producer
       const CUtensorMap* map = lane == 0 ? &p.tm_k : &p.tm_v;
       uint64_t* full = lane == 0 ? k_full : v_full;
@@ -334,14 +343,27 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
         for (int t = 0; t < 2; ++t)
           for (int c = max(0, kq[t] - 2); c < kq[t]; ++c) mbar_wait(&q_full[2 * t + (c & 1)], (c >> 1) & 1, p.error);
       }
-    } else if ((warp == 13 || warp == 15) && lane == 0) {
+#ifdef TLA_PREFILL_TRACE
+    } else if (warp == PP::kAllocWarp && lane == 0 && blockIdx.x == 0) {
+      // observer (trace builds): when S and P V of tile 0's first 16 steps complete
+      for (int c = 0; c < 16 && !*abort_flag; ++c) {
+        for (int i = 0; i < (1 << 24) && !mbar_test_wait(&s_full[0], c & 1); ++i) {
+        }
+        PPTRACE(c, 14);
+        for (int i = 0; i < (1 << 24) && !mbar_test_wait(&o_done[0], c & 1); ++i) {
+        }
+        PPTRACE(c, 15);
+      }
+#endif
+    } else if ((warp == PP::kSWarp || warp == PP::kPvWarp) && lane == 0) {
       // ============================================================ MMA issuers
-      // Warp 13 issues every S (both tiles), warp 15 every P V, so one
-      // thread's waits overlap the other's MMAs. S of a tile is issued once
+      // Warp 1 issues every S (both tiles), warp 3 every P V, so one
+      // thread's waits overlap the other's MMAs. Both poll their barriers
+      // without suspending (about 1% faster at config 3 than try_wait). S of a tile is issued once
       // that tile's softmax has read the previous S into registers (s_free);
       // P V once the softmax has stored P (p_full) and, for a tile's first
       // step of an item, once the epilogue has read that tile's O (o_free).
-      if (warp == 13) {
+      if (warp == PP::kSWarp) {
         constexpr uint32_t kIdS = idesc_f16(128, kT, false);
         const uint64_t dq = sdesc(smem_u32(smem + PP::kQ), 16, 1024);
         const uint64_t dk = sdesc(smem_u32(smem + PP::kK), 16, 1024);
@@ -360,7 +382,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
               if (jl < 0 || jl >= w.n[t]) continue;
               const int slot = 2 * t + (kq[t] & 1);
               if (jl == 0) spin(&q_full[slot], (kq[t] >> 1) & 1);
-              if (sc[t] > 0) wait(&s_free[t], (sc[t] - 1) & 1);
+              if (sc[t] > 0) spin(&s_free[t], (sc[t] - 1) & 1);
               tc_fence_after();
               const uint64_t qb = dq + static_cast<uint64_t>(slot * (PP::kTile >> 4));
               const uint64_t kb = dk + static_cast<uint64_t>(st * (PP::kTile >> 4));
@@ -396,8 +418,8 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
             for (int t = 0; t < 2; ++t) {
               const int jl = J - w.j0[t];
               if (jl < 0 || jl >= w.n[t]) continue;
-              if (jl == 0 && kq[t] > 0) wait(&o_free[t], (kq[t] - 1) & 1);
-              wait(&p_full[t], pc[t] & 1);
+              if (jl == 0 && kq[t] > 0) spin(&o_free[t], (kq[t] - 1) & 1);
+              spin(&p_full[t], pc[t] & 1);
               tc_fence_after();
               const uint64_t vb = dv + static_cast<uint64_t>(st * (PP::kTile >> 4));
               if (!*abort_flag) {
@@ -416,7 +438,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
         }
       }
     }
-  } else if (wg == 2) {
+  } else if (role == 2) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
     // ================================================================ epilogue
     // For each tile of each item: wait for its row sums and its last P V,
@@ -550,7 +572,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 184;" ::: "memory");
     // ================================================================ softmax
-    const int t = wg;          // this warpgroup's tile
+    const int t = role;        // this warpgroup's tile
     const int r = tid & 127;   // query row = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + PP::kS + 128 * t;
@@ -668,7 +690,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
       ++kq;
     }
 #ifdef TLA_PREFILL_TRACE
-    if (tid == 0 && blockIdx.x < 256) {
+    if (r == 0 && t == 0 && blockIdx.x < 256) {
       g_pp_cta[blockIdx.x][2] = globaltimer();
       g_pp_cta[blockIdx.x][4] = static_cast<unsigned long long>(c);
     }
