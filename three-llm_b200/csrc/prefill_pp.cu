@@ -52,9 +52,13 @@ using namespace prefill;
 #ifdef TLA_PREFILL_TRACE
 // Optional pipeline trace (builds with -DTLA_PREFILL_TRACE only): SM clock of
 // block 0's events, [step][event]; read with tla_debug_pp_trace. Softmax of
-// tile t (warp 4 t, per tile step): [5 t] S complete, [5 t + 1] S loaded,
-// [5 t + 2] maximum applied, [5 t + 3] P columns free, [5 t + 4] P stored.
-// Per union step: [10]/[11] S issue start/end, [12]/[13] P V issue start/end.
+// tile t (its first warp, per tile step): [5 t] S seen complete, [5 t + 1] S
+// loaded, [5 t + 2] maximum applied, [5 t + 3] exponentials done, [5 t + 4] P
+// stored. Per union step: [10]/[11] S issue start/end, [12]/[13] P V issue
+// start/end. An observer lane records [14] S of tile 0 complete and [15] P V
+// of tile 1 complete (first 16 steps). Such a trace showed S complete well
+// before the softmax reached its wait: the step's time outside the
+// exponentials is the softmax warps' own.
 __device__ unsigned long long g_pp_trace[64][16];
 // per CTA: globaltimer at entry, after set-up, when the softmax of tile 0
 // finished, at exit; and the union steps the CTA ran
@@ -345,12 +349,16 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
       }
 #ifdef TLA_PREFILL_TRACE
     } else if (warp == PP::kAllocWarp && lane == 0 && blockIdx.x == 0) {
-      // observer (trace builds): when S and P V of tile 0's first 16 steps complete
+      // observer (trace builds): when S of tile 0's first 16 steps completes
+      // ([14]) and when P V of tile 1 completes ([15], from a second lane)
       for (int c = 0; c < 16 && !*abort_flag; ++c) {
         for (int i = 0; i < (1 << 24) && !mbar_test_wait(&s_full[0], c & 1); ++i) {
         }
         PPTRACE(c, 14);
-        for (int i = 0; i < (1 << 24) && !mbar_test_wait(&o_done[0], c & 1); ++i) {
+      }
+    } else if (warp == PP::kAllocWarp && lane == 1 && blockIdx.x == 0) {
+      for (int c = 0; c < 16 && !*abort_flag; ++c) {
+        for (int i = 0; i < (1 << 24) && !mbar_test_wait(&o_done[1], c & 1); ++i) {
         }
         PPTRACE(c, 15);
       }
