@@ -77,8 +77,18 @@ __device__ unsigned long long g_proj_trace[1024][8];
   do {                                                                                    \
     if (threadIdx.x == 0 && blockIdx.x < 1024) g_proj_trace[blockIdx.x][(ev)] = globaltimer(); \
   } while (0)
+// out_allreduce_kernel per CTA: [0] entry, [1] after the wait, [2] own block
+// summed and sent, [3] exit; read with tla_debug_allreduce_trace
+__device__ unsigned long long g_ar_trace[256][4];
+#define ARTRACE(ev)                                                                     \
+  do {                                                                                  \
+    if (threadIdx.x == 0 && blockIdx.x < 256) g_ar_trace[blockIdx.x][(ev)] = globaltimer(); \
+  } while (0)
 #else
 #define PRTRACE(ev) \
+  do {              \
+  } while (0)
+#define ARTRACE(ev) \
   do {              \
   } while (0)
 #endif
@@ -561,19 +571,23 @@ cudaError_t launch_proj_t(tla_ctx* ctx, ProjParams& p, cudaStream_t stream) {
   return launch_pdl(proj_tc_kernel<D>, static_cast<unsigned>(tiles * p.ksplit), kThreads, smem, stream, p);
 }
 
-// Second half of the head-sharded output projection, one 128-thread CTA per SM
-// at most (every CTA a peer waits for is resident): each thread takes pairs of
-// this rank's column block, waits (bounded) for every rank's partial words of
-// the pair, sums them in rank order, adds bias and residual, keeps the result
-// and stores it into slot [this rank], second half, of every rank's buffer;
-// then it collects the other ranks' finished blocks. Every CTA finishes its
-// own block's pairs before it waits on another rank's.
+// Second half of the head-sharded output projection, one CTA per SM at most
+// (every CTA a peer waits for is resident), with blocks wide enough (up to
+// 512 threads) that each thread has about one pair: each thread takes pairs
+// of this rank's column block, loads the pair's bias and residual, waits
+// (bounded) for every rank's partial words of the pair, sums them in rank
+// order, adds bias and residual, keeps the result and stores it into slot
+// [this rank], second half, of every rank's buffer; then it collects the
+// other ranks' finished blocks. Every CTA finishes its own block's pairs
+// before it waits on another rank's.
 template <typename OUT>
-__global__ void __launch_bounds__(128) out_allreduce_kernel(ExchangeDev x, int rows, int hidden, int cols,
+__global__ void __launch_bounds__(512) out_allreduce_kernel(ExchangeDev x, int rows, int hidden, int cols,
                                                             const float* __restrict__ bias, const void* residual,
                                                             int res_f32, OUT* __restrict__ y, int* error) {
   __shared__ int epoch_s;
+  ARTRACE(0);
   griddep_wait();  // the partial tiles of this rank's GEMM are out
+  ARTRACE(1);
   const unsigned epoch = xch_epoch(x, &epoch_s);
   const uint8_t* mine = x.peers[x.rank] + static_cast<size_t>(epoch & 1u) * x.region_bytes;
   volatile int* abort_p = reinterpret_cast<volatile int*>(x.peers[x.rank] + 2 * x.region_bytes + 256);
@@ -614,6 +628,24 @@ __global__ void __launch_bounds__(128) out_allreduce_kernel(ExchangeDev x, int r
   };
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
     const int row = (2 * i) / cols, lc = 2 * i - row * cols, col = x.rank * cols + lc;
+    // bias and residual first: their loads overlap the wait for the partial words
+    float b0 = 0.f, b1 = 0.f;
+    if (bias) {
+      b0 = __ldg(bias + col);
+      b1 = __ldg(bias + col + 1);
+    }
+    if (residual) {
+      const size_t o = static_cast<size_t>(row) * hidden + col;
+      if (res_f32) {
+        const float2 q = *reinterpret_cast<const float2*>(static_cast<const float*>(residual) + o);
+        b0 += q.x;
+        b1 += q.y;
+      } else {
+        const __half2 q = *reinterpret_cast<const __half2*>(static_cast<const __half*>(residual) + o);
+        b0 += __low2float(q);
+        b1 += __high2float(q);
+      }
+    }
     uint4 w[kXchMaxRanks];
     wait_words(w, static_cast<size_t>(2 * i));
     float s0 = 0.f, s1 = 0.f;
@@ -623,28 +655,15 @@ __global__ void __launch_bounds__(128) out_allreduce_kernel(ExchangeDev x, int r
         s0 += __uint_as_float(w[r].x);
         s1 += __uint_as_float(w[r].z);
       }
-    if (bias) {
-      s0 += __ldg(bias + col);
-      s1 += __ldg(bias + col + 1);
-    }
-    if (residual) {
-      const size_t o = static_cast<size_t>(row) * hidden + col;
-      if (res_f32) {
-        const float2 q = *reinterpret_cast<const float2*>(static_cast<const float*>(residual) + o);
-        s0 += q.x;
-        s1 += q.y;
-      } else {
-        const __half2 q = *reinterpret_cast<const __half2*>(static_cast<const __half*>(residual) + o);
-        s0 += __low2float(q);
-        s1 += __high2float(q);
-      }
-    }
+    s0 += b0;
+    s1 += b1;
     store(row, col, s0, s1);
     const uint4 out = make_uint4(__float_as_uint(s0), epoch, __float_as_uint(s1), epoch);
     const size_t word = static_cast<size_t>(x.rank) * x.slot_words + half_words + 2 * i;
     for (int q = 0; q < x.ranks; ++q)
       if (q != x.rank) xch_st_v4(x.peers[q] + static_cast<size_t>(epoch & 1u) * x.region_bytes + word * 8, out);
   }
+  ARTRACE(2);
   for (int q = 0; q < x.ranks; ++q) {
     if (q == x.rank) continue;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
@@ -667,6 +686,7 @@ __global__ void __launch_bounds__(128) out_allreduce_kernel(ExchangeDev x, int r
     }
   }
   xch_finish(x, epoch);
+  ARTRACE(3);
 }
 
 }  // namespace
@@ -691,13 +711,15 @@ cudaError_t launch_out_proj_allreduce(tla_ctx* ctx, const ExchangeDev& x, const 
   cudaError_t e = launch_proj_t<64>(ctx, p, stream);
   if (e != cudaSuccess) return e;
   const int pairs = rows * p.cols / 2;
-  int grid = (pairs + 127) / 128;
+  int block = 128;  // widened until one pass of the grid covers every pair (at most 512)
+  while (block < 512 && static_cast<long long>(block) * ctx->sm_count < pairs) block *= 2;
+  int grid = (pairs + block - 1) / block;
   if (grid > ctx->sm_count) grid = ctx->sm_count;
   if (f32)
-    return launch_pdl(out_allreduce_kernel<float>, static_cast<unsigned>(grid), 128, 0, stream, x, rows, hidden,
-                      p.cols, bias, residual, 1, static_cast<float*>(y), ctx->d_error);
-  return launch_pdl(out_allreduce_kernel<__half>, static_cast<unsigned>(grid), 128, 0, stream, x, rows, hidden,
-                    p.cols, bias, residual, 0, static_cast<__half*>(y), ctx->d_error);
+    return launch_pdl(out_allreduce_kernel<float>, static_cast<unsigned>(grid), static_cast<unsigned>(block), 0,
+                      stream, x, rows, hidden, p.cols, bias, residual, 1, static_cast<float*>(y), ctx->d_error);
+  return launch_pdl(out_allreduce_kernel<__half>, static_cast<unsigned>(grid), static_cast<unsigned>(block), 0,
+                    stream, x, rows, hidden, p.cols, bias, residual, 0, static_cast<__half*>(y), ctx->d_error);
 }
 
 cudaError_t launch_qkv_proj(const tla_layer* L, const void* x, const void* weight, const float* bias, int hidden,
@@ -756,6 +778,9 @@ cudaError_t launch_out_proj(tla_ctx* ctx, const void* attn, const void* weight, 
 #ifdef TLA_PROJ_TRACE
 extern "C" int tla_debug_proj_trace(unsigned long long* host, int count) {
   return cudaMemcpyFromSymbol(host, tla::g_proj_trace, sizeof(unsigned long long) * count) == cudaSuccess ? 0 : -1;
+}
+extern "C" int tla_debug_allreduce_trace(unsigned long long* host, int count) {
+  return cudaMemcpyFromSymbol(host, tla::g_ar_trace, sizeof(unsigned long long) * count) == cudaSuccess ? 0 : -1;
 }
 #endif
 
