@@ -36,6 +36,7 @@ constexpr int kXStage = 128 * 128;  // x: 128 rows x 64 fp16 (one 128-byte row e
 constexpr int kWBox = 64 * 128;     // W: 64 rows of the reduction dim x 64 fp16 columns
 enum : int { kQkvDecode = 0, kQkvPrefill = 1, kOutProj = 2, kOutPush = 3 };
 
+
 struct ProjParams {
   CUtensorMap tm_x;  // [rows][K] fp16, box {64, 128}
   CUtensorMap tm_w;  // [K][N] fp16, box {64, 64}
@@ -242,6 +243,20 @@ __global__ void __launch_bounds__(kThreads, 2) proj_tc_kernel(const __grid_const
   const bool valid = row < p.rows;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
   if (p.ksplit > 1) {
+    // The output projection's epilogue inputs that do not depend on the
+    // other splits (this row's residual and bias columns) are brought into L1
+    // now, so that the last CTA's epilogue waits only on the workspace.
+    if (p.mode == kOutProj && valid) {
+      for (int c = set; c < p.NT / 32; c += 2) {
+        const size_t o = static_cast<size_t>(row) * p.N + n0 + 32 * c;
+        if (p.residual) {
+          const char* rp = static_cast<const char*>(p.residual) + o * (p.res_f32 ? 4 : 2);
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(rp));
+          if (p.res_f32) asm volatile("prefetch.global.L1 [%0];" ::"l"(rp + 64));
+        }
+        if (p.bias && r == 0) asm volatile("prefetch.global.L1 [%0];" ::"l"(p.bias + n0 + 32 * c));
+      }
+    }
     // add this CTA's partial tile into the workspace; the last CTA of the tile
     // goes on to the epilogue, reading the complete sums from the workspace
     for (int c = set; c < p.NT / 32; c += 2) {
