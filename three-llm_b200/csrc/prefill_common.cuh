@@ -50,17 +50,25 @@ __device__ __forceinline__ float ex2_poly(float x) {
 
 
 #ifndef TLA_PREFILL_POLY_EVERY
-#define TLA_PREFILL_POLY_EVERY 0  // every n-th pair of exponentials goes to the FMA pipe (0: none)
+#define TLA_PREFILL_POLY_EVERY 0  // head_dim 128 kernel: every n-th pair of exponentials on the FMA pipe (0: none)
+#endif
+#ifndef TLA_PP_POLY_EVERY
+// two-tile head_dim 64 kernel: every 8th pair of exponentials on the FMA pipe
+// (config 3: 0.0779 against 0.0780-0.0785 ms without; every 16th: 0.0788)
+#define TLA_PP_POLY_EVERY 8
 #endif
 
-// Whether pair `i` of a row's exponentials is evaluated with ex2_poly.
-__device__ __forceinline__ constexpr bool poly_pair(int i) {
-#if TLA_PREFILL_POLY_EVERY > 0
-  return i % TLA_PREFILL_POLY_EVERY == TLA_PREFILL_POLY_EVERY - 1;
-#else
-  return i < 0;
-#endif
+// Whether pair `i` of a row's exponentials is evaluated with ex2_poly, for
+// every EVERY-th pair (none when EVERY is 0).
+template <int EVERY>
+__device__ __forceinline__ constexpr bool poly_pair_every(int i) {
+  if constexpr (EVERY > 0) {
+    return i % EVERY == EVERY - 1;
+  } else {
+    return i < 0;
+  }
 }
+__device__ __forceinline__ constexpr bool poly_pair(int i) { return poly_pair_every<TLA_PREFILL_POLY_EVERY>(i); }
 
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two
 // columns' FMA or add, each element rounded as its scalar counterpart).

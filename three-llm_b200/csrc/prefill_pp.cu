@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(PP::kThreads, 1) prefill_pp_kernel(const __gri
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const int kc = 32 * h + i;
-            const bool poly = poly_pair(kc / 2);
+            const bool poly = poly_pair_every<TLA_PP_POLY_EVERY>(kc / 2);
             float x0, x1;
             fma_f32x2(__uint_as_float(sv[kc]), __uint_as_float(sv[kc + 1]), sl2x2, nmu2, x0, x1);
             const float e0 = poly ? ex2_poly(x0) : ex2(x0);
